@@ -1,0 +1,492 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention engine on tensorsmith's attention path.
+
+Workload ("c5"): long-context causal prefill + cached
+decode, bf16, B=32, H=32, D=128, T=32768 prefill then 128 decode steps, inputs
+~ N(0,1) from a seed, (batch, head) pairs sharded over the N GPUs of one node
+with no reduction and every output gathered to rank 0 over NCCL.  Total work
+is fixed as N grows (strong scaling).
+
+One step = prefill forward of the whole batch (tcgen05 kernel) + gather of O,
+then 128 x (KV append + split-K decode + gather of the token's output).
+
+Metric: prefill TFLOP/s & % bf16 peak; decode tokens/s & HBM
+GB/s.  ``value`` is whole-job prefill TFLOP/s (causal algorithmic FLOPs
+4*D*pairs / max-over-ranks device time); decode figures ride along under
+``decode``.  ``e2e`` repeats the step through the public API with pinned host
+inputs (H2D of Q/K/V and every decode token, D2H of O and decode outputs).
+
+``--impl reference`` times the reference algorithm (the NumPy port under
+oracle/, the reference being Python that cannot travel) on the host cores on a
+bounded sample of the same workload, and prints the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT), str(ROOT / "custom-ml-library_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "prefill TFLOP/s & % bf16 peak; decode tokens/s & HBM GB/s; at 1/2/4/8 GPUs"
+WORKLOADS = {
+    "c5": dict(batch=32, heads=32, head_dim=128, prefill=32768, decode_steps=128),
+    # reduced shape of the same kernels, for profiler captures only
+    "small": dict(batch=4, heads=32, head_dim=128, prefill=4096, decode_steps=4),
+}
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["engine", "reference"], default="engine")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c5")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
+    return ap.parse_args()
+
+
+def causal_flops(pairs: int, tq: int, tk: int, offset: int, d: int) -> float:
+    """Forward FLOPs 4*D*sum_i min(Tk, i+1+offset) over all (b,h) pairs."""
+    import numpy as np
+
+    i = np.arange(tq, dtype=np.int64)
+    return 4.0 * d * pairs * float(np.minimum(tk, i + 1 + offset).sum())
+
+
+def load_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return data, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+# --------------------------------------------------------------------------
+# clocks sampled during the timed region
+# --------------------------------------------------------------------------
+class ClockSampler:
+    def __init__(self, gpu_index: int):
+        self.proc = None
+        self.path = ROOT / "gpurun_out" / f"clocks_gpu{gpu_index}.csv"
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(gpu_index), "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        sm, mx, reasons = [], 0.0, set()
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                clock, cmax = float(parts[1]), float(parts[2])
+            except ValueError:
+                continue
+            sm.append(clock)
+            mx = max(mx, cmax)
+            names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        loaded = [c for c in sm if c > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------
+# reference arm / CPU baseline: the NumPy port of the reference algorithm
+# --------------------------------------------------------------------------
+def cpu_prefill_sample(cfg, rows: int, budget_s: float, seed: int = 0):
+    """Streaming-forward of the last ``rows`` queries of one (b,h) slice.
+
+    Returns (algorithmic FLOPs per rep, seconds per rep, reps)."""
+    import numpy as np
+
+    import oracle
+
+    t, d = cfg["prefill"], cfg["head_dim"]
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((1, 1, rows, d), dtype=np.float32)
+    k = rng.standard_normal((1, 1, t, d), dtype=np.float32)
+    v = rng.standard_normal((1, 1, t, d), dtype=np.float32)
+    flops = causal_flops(1, rows, t, t - rows, d)
+    times = []
+    start = time.perf_counter()
+    while not times or (time.perf_counter() - start < budget_s and len(times) < 50):
+        t0 = time.perf_counter()
+        oracle.attention_forward(q, k, v, is_causal=True, causal_offset=t - rows,
+                                 algorithm="streaming", block_size=2048)
+        times.append(time.perf_counter() - t0)
+    return flops, statistics.median(times), len(times)
+
+
+def cpu_decode_sample(cfg, pairs: int, reps: int = 3, seed: int = 1):
+    """One decode step for ``pairs`` (b,h) pairs against an fp16 cache of length T."""
+    import numpy as np
+
+    import oracle
+
+    t, d = cfg["prefill"], cfg["head_dim"]
+    rng = np.random.default_rng(seed)
+    k = rng.standard_normal((1, pairs, t, d)).astype(np.float16)
+    v = rng.standard_normal((1, pairs, t, d)).astype(np.float16)
+    q = rng.standard_normal((1, pairs, 1, d)).astype(np.float16)
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        oracle.attention_forward(q, k, v, is_causal=True, causal_offset=t - 1, algorithm="dense")
+        times.append(time.perf_counter() - t0)
+    per_pair = statistics.median(times) / pairs
+    bytes_per_pair = 2.0 * t * d * 2
+    return per_pair, bytes_per_pair
+
+
+def cpu_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(cfg, budget_s: float):
+    rows = 512
+    flops, sec, reps = cpu_prefill_sample(cfg, rows, budget_s)
+    per_pair, bpp = cpu_decode_sample(cfg, 2)
+    b, h = cfg["batch"], cfg["heads"]
+    return {
+        "value": flops / sec / 1e12,
+        "unit": "TFLOP/s",
+        "cores": cpu_cores(),
+        "kind": "port",
+        "sample": (f"oracle streaming forward (NumPy fp32, block 2048) of the last {rows} query rows of one "
+                   f"(b,h) slice vs T={cfg['prefill']} keys, median of {reps} reps; decode: 2 (b,h) pairs "
+                   f"x 1 token vs fp16 cache T={cfg['prefill']}"),
+        "decode_tokens_per_s": b / (per_pair * b * h),
+        "decode_gbs": bpp / per_pair / 1e9,
+    }
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    cfg = WORKLOADS[args.workload]
+    budget = max(2.0, min(args.cpu_seconds, 8.0))
+    values, decode = [], []
+    for step in range(args.warmup + args.steps):
+        base = cpu_baseline(cfg, budget if step >= args.warmup else 1.0)
+        if step >= args.warmup:
+            values.append(base["value"])
+            decode.append(base["decode_tokens_per_s"])
+    value = statistics.median(values)
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: causal prefill B={cfg['batch']} H={cfg['heads']} "
+                               f"D={cfg['head_dim']} T={cfg['prefill']} + {cfg['decode_steps']} decode steps",
+                   "sample": "bounded CPU sample, see cpu_baseline"},
+        "impl": "reference",
+        "decode": {"tokens_per_s": statistics.median(decode)},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cpu_cores(), "kind": "port",
+                         "sample": base["sample"]},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------
+# engine arm
+# --------------------------------------------------------------------------
+def run_engine(args, rank: int, world: int, local_rank: int):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from tensorsmith_b200 import engine
+    from tensorsmith_b200.distributed import ShardPlan, gather_to_root
+
+    cfg = WORKLOADS[args.workload]
+    B, H, D, T, S = cfg["batch"], cfg["heads"], cfg["head_dim"], cfg["prefill"], cfg["decode_steps"]
+    cap = T + S
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    plan = ShardPlan(B, H, world, rank)
+    n = plan.size  # pairs on this rank, laid out as [1, n, T, D]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    bf = torch.bfloat16
+
+    def randn(*shape):
+        return torch.randn(*shape, generator=gen, device=dev, dtype=torch.float32).to(bf)
+
+    q = randn(1, n, T, D)
+    kc = torch.zeros(1, n, cap, D, dtype=bf, device=dev)
+    vc = torch.zeros_like(kc)
+    kc[:, :, :T].copy_(randn(1, n, T, D))
+    vc[:, :, :T].copy_(randn(1, n, T, D))
+    o = torch.empty(1, n, T, D, dtype=bf, device=dev)
+    qd = randn(S, 1, n, 1, D)
+    kd = randn(S, 1, n, 1, D)
+    vd = randn(S, 1, n, 1, D)
+    od = torch.empty(S, 1, n, 1, D, dtype=bf, device=dev)
+    o_full = torch.empty(world, n, T, D, dtype=bf, device=dev) if rank == 0 and world > 1 else None
+    od_full = torch.empty(S, world, n, 1, D, dtype=bf, device=dev) if rank == 0 and world > 1 else None
+    ws = torch.empty(max(16, engine.decode_workspace_bytes(qd[0], kc[:, :, : T + 1], vc[:, :, : T + 1],
+                                                             is_causal=True, causal_offset=T)),
+                     dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize()
+
+    splits = engine.decode_workspace_bytes(qd[0], kc[:, :, :cap], vc[:, :, :cap], is_causal=True,
+                                           causal_offset=cap - 1) > 0
+    launches_per_step = 1 + S * (2 + (1 if splits else 0))
+
+    def gather(src, dst):
+        if world > 1:
+            gather_to_root(src, plan, out=dst)
+
+    def step(ev):
+        ev[0].record()
+        engine.forward(q, kc[:, :, :T], vc[:, :, :T], is_causal=True, need_lse=False, out=o)
+        ev[1].record()
+        gather(o, o_full)
+        ev[2].record()
+        for s in range(S):
+            engine.kv_append(kd[s], vd[s], kc, vc, position=T + s)
+            engine.decode(qd[s], kc[:, :, : T + s + 1], vc[:, :, : T + s + 1], is_causal=True,
+                          causal_offset=T + s, out=od[s], workspace=ws)
+            gather(od[s], None if od_full is None else od_full[s])
+        ev[3].record()
+
+    def new_events():
+        return [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step(new_events())
+    barrier()
+    engine.check_device_status(dev)
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    barrier()
+    evs = [new_events() for _ in range(args.steps)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_stop = torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for ev in evs:
+        step(ev)
+    t_stop.record()
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    engine.check_device_status(dev)
+
+    kern_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    prefill_ms = [e[0].elapsed_time(e[2]) for e in evs]
+    decode_ms = [e[2].elapsed_time(e[3]) for e in evs]
+    total_ms = t_start.elapsed_time(t_stop)
+    local = torch.tensor([statistics.mean(kern_ms), statistics.mean(prefill_ms),
+                          statistics.mean(decode_ms), total_ms / args.steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(local, op=dist.ReduceOp.MAX)
+    kern, pre, dec, step_ms = local.tolist()
+
+    flops = causal_flops(B * H, T, T, 0, D)
+    flops_rank = causal_flops(n, T, T, 0, D)
+    value = flops / (pre / 1e3) / 1e12
+    lens = np.arange(T + 1, T + S + 1)
+    kv_bytes = float(2 * B * H * D * 2 * lens.sum())  # K and V bf16 reads over all decode steps
+    dec_tokens = B * S / (dec / 1e3)
+    peaks, peak_src = load_peaks()
+
+    # --- e2e through the public API with pinned host buffers ----------------
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, cfg, plan, rank, world, local_rank, q, kc, vc, qd, kd, vd, ws, barrier, gather)
+
+    result = None
+    if rank == 0:
+        achieved = flops_rank / (kern / 1e3) / 1e12
+        peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+        result = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": step_ms,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {
+                "workload": (f"{args.workload}: causal prefill bf16 B={B} H={H} D={D} T={T}, then {S} decode "
+                             f"steps (KV append + split-K decode), (b,h) pairs sharded over {world} GPU(s), "
+                             "outputs gathered to rank 0 over NCCL"),
+                "global_batch": B, "seq_len": T, "parallelism": f"bxh-shard{world}",
+                "l2": "inputs larger than L2 (Q/K/V/cache >= 8 GB per step)",
+            },
+            "prefill": {"tflops": value, "frac_of_measured_bf16_sustained": value / world / peak,
+                        "frac_of_nominal_2250": value / world / 2250.0, "ms": pre,
+                        "kernel_ms": kern, "gather_ms": pre - kern},
+            "decode": {"tokens_per_s": dec_tokens, "hbm_gbs": kv_bytes / (dec / 1e3) / 1e9,
+                       "hbm_gbs_per_gpu": kv_bytes / world / (dec / 1e3) / 1e9,
+                       "frac_of_measured_hbm": kv_bytes / world / (dec / 1e3) / 1e9 / peaks["hbm_gbs"],
+                       "ms_per_token_step": dec / S},
+            "roofline": {"bound": "tensor", "kernel": "tc_fwd_kernel<128,bf16>", "achieved": achieved,
+                         "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                         "peak_source": f"{peak_src} bf16_tflops_sustained",
+                         "traffic": None,
+                         "algorithmic": f"4*D*causal_pairs = {flops_rank:.4g} FLOP per launch on rank 0"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+        }
+        if e2e is not None:
+            result["e2e"] = e2e
+        if world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
+    return result
+
+
+def run_e2e(args, cfg, plan, rank, world, local_rank, q, kc, vc, qd, kd, vd, ws, barrier, gather):
+    """The same step through the public API with inputs in pinned host memory."""
+    import torch
+
+    from tensorsmith_b200 import engine
+
+    B, H, D, T, S = cfg["batch"], cfg["heads"], cfg["head_dim"], cfg["prefill"], cfg["decode_steps"]
+    dev = q.device
+    n = plan.size
+    try:
+        hq = torch.empty_like(q, device="cpu").pin_memory()
+        hk = torch.empty(1, n, T, D, dtype=q.dtype).pin_memory()
+        hv = torch.empty_like(hk).pin_memory()
+        ho = torch.empty((world if rank == 0 else 1) * n * T * D, dtype=q.dtype).pin_memory()
+        hqd = torch.empty_like(qd, device="cpu").pin_memory()
+        hkd = torch.empty_like(kd, device="cpu").pin_memory()
+        hvd = torch.empty_like(vd, device="cpu").pin_memory()
+        hod = torch.empty((S, world if rank == 0 else 1, n, 1, D), dtype=q.dtype).pin_memory()
+    except RuntimeError as error:
+        return {"value": None, "unit": "TFLOP/s", "note": f"pinned host allocation failed: {error}"}
+    hq.copy_(q.cpu())
+    hk.copy_(kc[:, :, :T].cpu())
+    hv.copy_(vc[:, :, :T].cpu())
+    hqd.copy_(qd.cpu())
+    hkd.copy_(kd.cpu())
+    hvd.copy_(vd.cpu())
+    dq = torch.empty_like(q)
+    do = torch.empty_like(q)
+    o_full = torch.empty(world, n, T, D, dtype=q.dtype, device=dev) if rank == 0 and world > 1 else None
+    dqd = torch.empty_like(qd)
+    dod = torch.empty_like(qd)
+    od_full = torch.empty(S, world, n, 1, D, dtype=q.dtype, device=dev) if rank == 0 and world > 1 else None
+
+    def step():
+        dq.copy_(hq, non_blocking=True)
+        kc[:, :, :T].copy_(hk, non_blocking=True)
+        vc[:, :, :T].copy_(hv, non_blocking=True)
+        dqd.copy_(hqd, non_blocking=True)
+        engine.forward(dq, kc[:, :, :T], vc[:, :, :T], is_causal=True, need_lse=False, out=do)
+        gather(do, o_full)
+        if rank == 0:
+            ho.view(-1).copy_((o_full if o_full is not None else do).view(-1), non_blocking=True)
+        for s in range(S):
+            kd_s = hkd[s].to(dev, non_blocking=True)
+            vd_s = hvd[s].to(dev, non_blocking=True)
+            engine.kv_append(kd_s, vd_s, kc, vc, position=T + s)
+            engine.decode(dqd[s], kc[:, :, : T + s + 1], vc[:, :, : T + s + 1], is_causal=True,
+                          causal_offset=T + s, out=dod[s], workspace=ws)
+            gather(dod[s], None if od_full is None else od_full[s])
+            if rank == 0:
+                hod[s].copy_((od_full[s] if od_full is not None else dod[s]).view(hod[s].shape),
+                             non_blocking=True)
+
+    steps = max(1, min(args.steps, 2))
+    step()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(steps):
+        step()
+    ev1.record()
+    barrier()
+    import torch.distributed as dist
+
+    ms = torch.tensor([ev0.elapsed_time(ev1) / steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = ms.item()
+    flops = causal_flops(B * H, T, T, 0, D)
+    esz = q.element_size()
+    h2d = (3 * n * T * D + 3 * S * n * D) * esz
+    d2h = (world * n * T * D + S * world * n * D) * esz if rank == 0 else 0
+    return {"value": flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+            "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h, "steps": steps,
+            "path": "tensorsmith_b200.engine (C ABI) with pinned host inputs/outputs"}
+
+
+def main():
+    args = parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if world != args.gpus and "RANK" in os.environ:
+        args.gpus = world
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        result = run_engine(args, rank, world, local_rank)
+        if rank == 0 and result is not None:
+            print(json.dumps(result), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,156 @@
+// extern "C" entry points of libts_attn.so (declared in include/ts_attn.h):
+// argument validation, kernel selection and the device fault word.
+#include <cstdio>
+
+#include "common.cuh"
+#include "decode.cuh"
+#include "kv_cache.cuh"
+#include "simt.cuh"
+#include "tc_fwd.cuh"
+
+namespace {
+
+// Fault word written by kernels whose bounded waits gave up (per device).
+__device__ uint32_t g_fault_word;
+
+uint32_t* fault_ptr() {
+  static uint32_t* ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_fault_word) != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<uint32_t*>(p);
+  }
+  return ptrs[dev];
+}
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+int from_cuda(cudaError_t e) {
+  if (e == cudaSuccess) return TS_OK;
+  if (e == cudaErrorInvalidValue) return TS_ERR_INVALID_ARGUMENT;
+  return TS_ERR_LAUNCH;
+}
+
+bool dtype_ok(int d) { return d == TS_F32 || d == TS_F16 || d == TS_BF16 || d == TS_F64; }
+
+int check_params(const ts_attn_params* p) {
+  if (!p) return TS_ERR_INVALID_ARGUMENT;
+  if (!dtype_ok(p->dtype)) return TS_ERR_UNSUPPORTED;
+  if (p->batch <= 0 || p->q_heads <= 0 || p->kv_heads <= 0 || p->q_len <= 0 || p->kv_len <= 0 ||
+      p->head_dim <= 0 || p->value_dim <= 0)
+    return TS_ERR_INVALID_ARGUMENT;
+  if (p->q_heads % p->kv_heads) return TS_ERR_INVALID_ARGUMENT;
+  if (p->head_dim > 256 || p->value_dim > 256) return TS_ERR_UNSUPPORTED;
+  if (!p->q.data || !p->k.data || !p->v.data || !p->o.data) return TS_ERR_INVALID_ARGUMENT;
+  if (p->causal_offset < 0) return TS_ERR_INVALID_ARGUMENT;
+  if (!(p->scale == p->scale) || p->scale > 3.0e38f || p->scale < -3.0e38f) return TS_ERR_INVALID_ARGUMENT;
+  if (p->mask_kind < TS_MASK_NONE || p->mask_kind > TS_MASK_ADD_F32) return TS_ERR_INVALID_ARGUMENT;
+  if (p->mask_kind != TS_MASK_NONE && !p->mask) return TS_ERR_INVALID_ARGUMENT;
+  return TS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ts_attn_abi_version(void) { return TS_ATTN_ABI_VERSION; }
+
+const char* ts_attn_strerror(int status) {
+  switch (status) {
+    case TS_OK: return "ok";
+    case TS_ERR_INVALID_ARGUMENT: return "invalid argument (shape, stride, pointer or value)";
+    case TS_ERR_UNSUPPORTED: return "unsupported dtype / dimension combination";
+    case TS_ERR_WORKSPACE: return "workspace missing or too small";
+    case TS_ERR_LAUNCH: return "CUDA kernel launch or driver call failed";
+    case TS_ERR_DEVICE_TIMEOUT: return "a bounded wait inside an engine kernel gave up";
+    case TS_ERR_CAPACITY: return "KV-cache capacity exceeded or empty append";
+  }
+  return "unknown status";
+}
+
+int ts_attn_fwd_path(const ts_attn_params* p, int decode) {
+  const int st = check_params(p);
+  if (st != TS_OK) return st;
+  if (decode && tsa::decode_supported(*p)) return TS_PATH_DECODE;
+  if (tsa::tc_fwd_supported(*p)) return TS_PATH_TCGEN05;
+  return TS_PATH_SIMT;
+}
+
+int ts_attn_fwd(const ts_attn_params* p, void* stream) {
+  const int st = check_params(p);
+  if (st != TS_OK) return st;
+  if (tsa::tc_fwd_supported(*p)) return from_cuda(tsa::tc_forward(*p, fault_ptr(), as_stream(stream)));
+  return from_cuda(tsa::simt_forward(*p, as_stream(stream)));
+}
+
+size_t ts_attn_decode_workspace_size(const ts_attn_params* p) {
+  if (check_params(p) != TS_OK || !tsa::decode_supported(*p)) return 0;
+  return tsa::decode_workspace(*p);
+}
+
+int ts_attn_decode(const ts_attn_params* p, void* workspace, size_t workspace_bytes, void* stream) {
+  const int st = check_params(p);
+  if (st != TS_OK) return st;
+  if (!tsa::decode_supported(*p)) return from_cuda(tsa::simt_forward(*p, as_stream(stream)));
+  const size_t need = tsa::decode_workspace(*p);
+  if (need && (!workspace || workspace_bytes < need)) return TS_ERR_WORKSPACE;
+  return from_cuda(tsa::decode_forward(*p, workspace, workspace_bytes, fault_ptr(), as_stream(stream)));
+}
+
+size_t ts_attn_bwd_workspace_size(const ts_attn_bwd_params* bp) {
+  if (!bp || check_params(&bp->fwd) != TS_OK) return 0;
+  return tsa::simt_backward_workspace(*bp);
+}
+
+int ts_attn_bwd(const ts_attn_bwd_params* bp, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!bp) return TS_ERR_INVALID_ARGUMENT;
+  const int st = check_params(&bp->fwd);
+  if (st != TS_OK) return st;
+  if (!bp->fwd.lse || !bp->dout.data || !bp->dq.data || !bp->dk.data || !bp->dv.data)
+    return TS_ERR_INVALID_ARGUMENT;
+  const size_t need = tsa::simt_backward_workspace(*bp);
+  if (!workspace || workspace_bytes < need) return TS_ERR_WORKSPACE;
+  return from_cuda(tsa::simt_backward(*bp, workspace, as_stream(stream)));
+}
+
+int ts_kv_append(const ts_kv_append_params* p, void* stream) {
+  if (!p) return TS_ERR_INVALID_ARGUMENT;
+  if (!dtype_ok(p->src_dtype) || !dtype_ok(p->cache_dtype)) return TS_ERR_UNSUPPORTED;
+  if (p->batch <= 0 || p->heads <= 0 || p->head_dim <= 0 || p->value_dim <= 0 || p->capacity <= 0)
+    return TS_ERR_INVALID_ARGUMENT;
+  if (!p->key.data || !p->value.data || !p->key_cache.data || !p->value_cache.data)
+    return TS_ERR_INVALID_ARGUMENT;
+  if (p->steps <= 0) return TS_ERR_CAPACITY;
+  if (!p->positions && (p->position < 0 || p->position + p->steps > p->capacity)) return TS_ERR_CAPACITY;
+  return from_cuda(tsa::kv_append(*p, as_stream(stream)));
+}
+
+int ts_kv_reorder(ts_view4 src, ts_view4 dst, int32_t dtype, int32_t batch, int32_t heads, int32_t length,
+                  int32_t channels, const int32_t* index, void* stream) {
+  if (!dtype_ok(dtype)) return TS_ERR_UNSUPPORTED;
+  if (!src.data || !dst.data || !index || batch <= 0 || heads <= 0 || length < 0 || channels <= 0)
+    return TS_ERR_INVALID_ARGUMENT;
+  return from_cuda(tsa::kv_reorder(src, dst, dtype, batch, heads, length, channels, index, as_stream(stream)));
+}
+
+int ts_attn_device_status(void* stream, uint32_t* info) {
+  uint32_t* f = fault_ptr();
+  if (!f) return TS_ERR_LAUNCH;
+  uint32_t host = 0;
+  cudaStream_t s = as_stream(stream);
+  if (cudaMemcpyAsync(&host, f, sizeof(uint32_t), cudaMemcpyDeviceToHost, s) != cudaSuccess) return TS_ERR_LAUNCH;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return TS_ERR_LAUNCH;
+  if (info) *info = host;
+  if (host) {
+    const uint32_t zero = 0;
+    if (cudaMemcpyAsync(f, &zero, sizeof(uint32_t), cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+      return TS_ERR_LAUNCH;
+    return TS_ERR_DEVICE_TIMEOUT;
+  }
+  return TS_OK;
+}
+
+}  // extern "C"

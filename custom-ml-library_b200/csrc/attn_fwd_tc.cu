@@ -1,0 +1,459 @@
+// Causal / full prefill attention forward on the 5th-generation tensor cores
+// (tcgen05) for bf16 / f16 inputs with D = Dv in {64, 128}.
+//
+// Replaces the dense / streaming forwards of tensorsmith's nn/attention.py
+// (:132-145, :175-198) and fills the vendor "native" slot (:146-174) on CUDA:
+// the same online-softmax recurrence (running max, running sum, rescaled
+// accumulator; output a/l; LSE = m + log l), computed tile by tile without
+// materialising P in HBM and skipping key tiles the causal rule hides.
+//
+// One CTA = one 128-row query tile of one (batch, head).  Warp roles:
+//   warp 0   TMA producer: Q once, then K/V 128-key tiles into 2-stage rings
+//            (separate K and V rings so K(j+2) can land while P(j).V(j) runs)
+//   warp 1   MMA issuer (one thread): S = Q K^T into a double-buffered TMEM S,
+//            O += P V into TMEM O; completion signalled with tcgen05.commit
+//   warp 2   TMEM allocator (512 columns: S0 | S1 | O)
+//   warps 4-7 softmax warpgroup: thread r owns query row r (TMEM lane r):
+//            loads its S row (tcgen05.ld), exp2-domain online softmax with lazy
+//            rescaling (O is only rescaled when the running max grows by more
+//            than 2^8), writes P (bf16/f16) into a 128B-swizzled shared tile,
+//            then the epilogue O / l -> global and the LSE.
+// Shared-memory operands use the canonical 128-byte-swizzle layouts: Q, K and
+// P are K-major (8-row x 128-byte atoms, 1024 B apart); V is read MN-major
+// (64-channel blocks 16 KB apart, 8-key groups 1024 B apart).  No TMA load
+// uses cluster multicast.
+#include <type_traits>
+
+#include "ptx.cuh"
+#include "tc_fwd.cuh"
+
+namespace tsa {
+
+namespace {
+
+constexpr int kBM = 128, kBN = 128;
+constexpr int kSlabBytes = 128 * 128;  // 128 rows x 128 bytes
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+template <int D> struct Cfg {
+  static constexpr int kSlabs = D / 64;
+  static constexpr int kStages = D == 64 ? 3 : 2;
+  static constexpr int kTileBytes = kSlabs * kSlabBytes;  // one 128-row Q/K/V tile
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffK = kOffQ + kTileBytes;
+  static constexpr int kOffV = kOffK + kStages * kTileBytes;
+  static constexpr int kOffP = kOffV + kStages * kTileBytes;
+  static constexpr int kOffBar = kOffP + 2 * kSlabBytes;
+  static constexpr int kBarBytes = 256;
+  static constexpr int kSmem = kOffBar + kBarBytes + 1024;  // +1024 alignment slack
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kColS = 0;     // two 128-column S buffers
+  static constexpr uint32_t kColO = 256;   // D columns
+};
+
+struct Bars {
+  uint64_t q_full;
+  uint64_t k_full[3], k_empty[3];
+  uint64_t v_full[3], v_empty[3];
+  uint64_t s_full[2];
+  uint64_t p_full;
+  uint64_t o_done;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+struct TcFwdArgs {
+  ts_attn_params p;
+  int n_q_tiles;
+  uint32_t* fault;
+};
+
+__device__ __forceinline__ bool fault_set(const uint32_t* fault) {
+  return fault && *reinterpret_cast<const volatile uint32_t*>(fault) != 0u;
+}
+
+// Bounded wait that also gives up as soon as any CTA recorded a fault.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, uint32_t* fault,
+                                         uint32_t site) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0u) {
+      if (fault_set(fault)) return false;
+      if (global_ns() - t0 > kWaitLimitNs) {
+        record_fault(fault, site);
+        return false;
+      }
+    }
+  }
+}
+
+}  // namespace
+
+template <int D, bool kBF16>
+__global__ void __launch_bounds__(256, 1)
+    tc_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                  const __grid_constant__ CUtensorMap tm_v, TcFwdArgs args) {
+  using C = Cfg<D>;
+  const ts_attn_params& p = args.p;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + C::kOffBar);
+  unsigned char* sQ = smem + C::kOffQ;
+  unsigned char* sK = smem + C::kOffK;
+  unsigned char* sV = smem + C::kOffV;
+  unsigned char* sP = smem + C::kOffP;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q_tile = args.n_q_tiles - 1 - (int)blockIdx.x;  // longest causal tiles first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (p.q_heads / p.kv_heads);
+
+  // Visible key range of this tile.
+  int kv_end = p.kv_len;
+  int64_t offset = p.causal_offset;
+  if (p.kv_lens) {
+    kv_end = min(kv_end, max(0, p.kv_lens[b]));
+    offset = (int64_t)kv_end - p.q_len;
+  }
+  const int q0 = q_tile * kBM;
+  const int q_last = min(q0 + kBM - 1, p.q_len - 1);
+  int kv_lim = kv_end;
+  if (p.is_causal) kv_lim = (int)i64max(0, i64min(kv_end, (int64_t)q_last + offset + 1));
+  const int n_tiles = ceil_div(kv_lim, kBN);
+  const bool dead = fault_set(args.fault);
+
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(&bars->q_full, 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      ptx::mbar_init(&bars->k_full[s], 1);
+      ptx::mbar_init(&bars->k_empty[s], 1);
+      ptx::mbar_init(&bars->v_full[s], 1);
+      ptx::mbar_init(&bars->v_empty[s], 1);
+    }
+    ptx::mbar_init(&bars->s_full[0], 1);
+    ptx::mbar_init(&bars->s_full[1], 1);
+    ptx::mbar_init(&bars->p_full, 4);
+    ptx::mbar_init(&bars->o_done, 1);
+    ptx::mbar_init(&bars->drain, 1);
+    bars->abort = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 2) {
+    ptx::tmem_alloc(&bars->tmem_base, C::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0 && n_tiles > 0 && !dead) {
+      ptx::prefetch_tensormap(&tm_q);
+      ptx::prefetch_tensormap(&tm_k);
+      ptx::prefetch_tensormap(&tm_v);
+      ptx::mbar_expect_tx(&bars->q_full, C::kTileBytes);
+      for (int s = 0; s < C::kSlabs; ++s)
+        ptx::tma_load_4d(sQ + s * kSlabBytes, &tm_q, 64 * s, q0, h, b, &bars->q_full);
+      int k_issued = 0, v_issued = 0;
+      for (int j = 0; j < n_tiles; ++j) {
+        const int s = j % C::kStages;
+        const uint32_t ph = ((j / C::kStages) - 1) & 1;
+        if (j >= C::kStages && !wait_bar(&bars->k_empty[s], ph, args.fault, FAULT_FWD_EMPTY)) break;
+        ptx::mbar_expect_tx(&bars->k_full[s], C::kTileBytes);
+        for (int sl = 0; sl < C::kSlabs; ++sl)
+          ptx::tma_load_4d(sK + (s * C::kSlabs + sl) * kSlabBytes, &tm_k, 64 * sl, j * kBN, hk, b,
+                           &bars->k_full[s]);
+        k_issued = j + 1;
+        if (j >= C::kStages && !wait_bar(&bars->v_empty[s], ph, args.fault, FAULT_FWD_EMPTY)) break;
+        ptx::mbar_expect_tx(&bars->v_full[s], C::kTileBytes);
+        for (int sl = 0; sl < C::kSlabs; ++sl)
+          ptx::tma_load_4d(sV + (s * C::kSlabs + sl) * kSlabBytes, &tm_v, 64 * sl, j * kBN, hk, b,
+                           &bars->v_full[s]);
+        v_issued = j + 1;
+      }
+      // Drain: every issued copy must have landed before shared memory is released.
+      (void)wait_bar(&bars->q_full, 0, nullptr, FAULT_FWD_DRAIN);
+      for (int j = max(0, k_issued - C::kStages); j < k_issued; ++j)
+        (void)wait_bar(&bars->k_full[j % C::kStages], (j / C::kStages) & 1, nullptr, FAULT_FWD_DRAIN);
+      for (int j = max(0, v_issued - C::kStages); j < v_issued; ++j)
+        (void)wait_bar(&bars->v_full[j % C::kStages], (j / C::kStages) & 1, nullptr, FAULT_FWD_DRAIN);
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ----------------------------
+    if (lane == 0 && n_tiles > 0 && !dead) {
+      constexpr uint32_t idesc_qk = ptx::idesc_f16(kBF16, kBM, kBN, false, false);
+      constexpr uint32_t idesc_pv = ptx::idesc_f16(kBF16, kBM, D, false, true);
+      const uint32_t sQa = ptx::smem_u32(sQ), sKa = ptx::smem_u32(sK), sVa = ptx::smem_u32(sV),
+                     sPa = ptx::smem_u32(sP);
+      bool ok = wait_bar(&bars->q_full, 0, args.fault, FAULT_FWD_Q);
+      ptx::tc_fence_after();
+      auto issue_pv = [&](int jj) -> bool {
+        if (!wait_bar(&bars->p_full, jj & 1, args.fault, FAULT_FWD_P)) return false;
+        const int s = jj % C::kStages;
+        if (!wait_bar(&bars->v_full[s], (jj / C::kStages) & 1, args.fault, FAULT_FWD_KV)) return false;
+        ptx::tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t a = ptx::sw128_desc(sPa + (kk >> 2) * kSlabBytes + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd =
+              ptx::sw128_desc(sVa + s * C::kTileBytes + kk * 16 * 128, kSlabBytes, 1024);
+          ptx::mma_f16_ss(tmem + C::kColO, a, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+        }
+        ptx::mma_commit(&bars->o_done);
+        ptx::mma_commit(&bars->v_empty[s]);
+        return true;
+      };
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int s = j % C::kStages;
+        if (!wait_bar(&bars->k_full[s], (j / C::kStages) & 1, args.fault, FAULT_FWD_KV)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d_s = tmem + C::kColS + (uint32_t)(j & 1) * kBN;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kSlabBytes + (kk & 3) * 32;
+          const uint64_t a = ptx::sw128_desc(sQa + off, 16, 1024);
+          const uint64_t bd = ptx::sw128_desc(sKa + s * C::kTileBytes + off, 16, 1024);
+          ptx::mma_f16_ss(d_s, a, bd, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        ptx::mma_commit(&bars->s_full[j & 1]);
+        ptx::mma_commit(&bars->k_empty[s]);
+        if (j >= 1 && !issue_pv(j - 1)) ok = false;
+      }
+      if (ok) ok = issue_pv(n_tiles - 1);
+      // Drain: wait until every issued MMA has completed.
+      ptx::mma_commit(&bars->drain);
+      (void)wait_bar(&bars->drain, 0, nullptr, FAULT_FWD_DRAIN);
+      if (!ok) atomicExch(&bars->abort, 1);
+    }
+  } else if (warp >= 4) {
+    // ------------------------- softmax warpgroup ---------------------------
+    const int row = (warp - 4) * 32 + lane;
+    const int qi = q0 + row;
+    const uint32_t t_row = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const float qk_scale = p.scale * kLog2e;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = !dead;
+    for (int j = 0; j < n_tiles && ok; ++j) {
+      if (!wait_bar(&bars->s_full[j & 1], (j >> 1) & 1, args.fault, FAULT_FWD_S)) {
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      float x[kBN];
+      {
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < kBN / 32; ++c) {
+          ptx::tmem_ld32(t_row + C::kColS + (uint32_t)(j & 1) * kBN + 32 * c, r);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) x[32 * c + e] = __uint_as_float(r[e]) * qk_scale;
+        }
+      }
+      const int k0 = j * kBN;
+      const bool need_mask = (k0 + kBN > kv_end) || (p.is_causal && (int64_t)k0 + kBN - 1 > (int64_t)q0 + offset);
+      if (need_mask) {
+        const int64_t lim = p.is_causal ? (int64_t)qi + offset : (int64_t)kv_end;
+#pragma unroll
+        for (int c = 0; c < kBN; ++c) {
+          const int key = k0 + c;
+          const bool vis = key < kv_end && (int64_t)key <= lim;
+          x[c] = vis ? x[c] : -INFINITY;
+        }
+      }
+      float mx = x[0];
+#pragma unroll
+      for (int c = 1; c < kBN; ++c) mx = fmaxf(mx, x[c]);
+      const float m_new = fmaxf(m_run, mx);
+      const bool rescale = m_new > m_run + kRescaleThreshold ||
+                           (m_run == -INFINITY && m_new != -INFINITY);
+      float factor = 1.f;
+      if (rescale) {
+        factor = m_run == -INFINITY ? 0.f : ptx::ex2(m_run - m_new);
+        m_run = m_new;
+        l_run *= factor;
+      }
+      const float safe = m_run == -INFINITY ? 0.f : m_run;
+      uint32_t pk[kBN / 2];
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < kBN; c += 2) {
+        const float p0 = ptx::ex2(x[c] - safe), p1 = ptx::ex2(x[c + 1] - safe);
+        sum += p0 + p1;
+        pk[c / 2] = kBF16 ? ptx::pack_bf16(p0, p1) : ptx::pack_f16(p0, p1);
+      }
+      l_run += sum;
+      // P buffer and O are free once P(j-1).V(j-1) has completed.
+      if (j >= 1 && !wait_bar(&bars->o_done, (j - 1) & 1, args.fault, FAULT_FWD_O)) {
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      if (rescale && j >= 1) {
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          ptx::tmem_ld32(t_row + C::kColO + 32 * c, r);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * factor);
+          ptx::tmem_st32(t_row + C::kColO + 32 * c, r);
+        }
+        ptx::tmem_wait_st();
+      }
+      // P row -> 128B-swizzled K-major tile: slab = 64 keys, 16-byte chunk c at (c ^ row%8).
+#pragma unroll
+      for (int sl = 0; sl < 2; ++sl) {
+        unsigned char* rowp = sP + sl * kSlabBytes + row * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const int w = sl * 32 + c * 4;
+          uint4 v = make_uint4(pk[w], pk[w + 1], pk[w + 2], pk[w + 3]);
+          *reinterpret_cast<uint4*>(rowp + ((c ^ (row & 7)) << 4)) = v;
+        }
+      }
+      ptx::fence_proxy_async_smem();
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&bars->p_full);
+    }
+    if (ok && n_tiles > 0) ok = wait_bar(&bars->o_done, (n_tiles - 1) & 1, args.fault, FAULT_FWD_O);
+    ptx::tc_fence_after();
+    // Epilogue: O / l -> global, LSE.
+    const bool live_row = qi < p.q_len;
+    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+    using T = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
+    T* orow = reinterpret_cast<T*>(p.o.data) + (int64_t)b * p.o.stride[0] + (int64_t)h * p.o.stride[1] +
+              (int64_t)qi * p.o.stride[2];
+#pragma unroll
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t r[32];
+      if (n_tiles > 0 && ok) {
+        ptx::tmem_ld32(t_row + C::kColO + 32 * c, r);
+        ptx::tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) r[e] = 0u;
+      }
+      if (live_row) {
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          uint4 v;
+          const float* f = reinterpret_cast<const float*>(r + e);
+          if (kBF16) {
+            v = make_uint4(ptx::pack_bf16(f[0] * inv, f[1] * inv), ptx::pack_bf16(f[2] * inv, f[3] * inv),
+                           ptx::pack_bf16(f[4] * inv, f[5] * inv), ptx::pack_bf16(f[6] * inv, f[7] * inv));
+          } else {
+            v = make_uint4(ptx::pack_f16(f[0] * inv, f[1] * inv), ptx::pack_f16(f[2] * inv, f[3] * inv),
+                           ptx::pack_f16(f[4] * inv, f[5] * inv), ptx::pack_f16(f[6] * inv, f[7] * inv));
+          }
+          *reinterpret_cast<uint4*>(orow + 32 * c + e) = v;
+        }
+      }
+    }
+    if (live_row && p.lse)
+      reinterpret_cast<float*>(p.lse)[(int64_t)b * p.lse_stride[0] + (int64_t)h * p.lse_stride[1] + (int64_t)qi * p.lse_stride[2]] =
+          l_run > 0.f ? (m_run + __log2f(l_run)) * kLn2 : -INFINITY;
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                  CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+static bool view_tma_ok(const ts_view4& v) {
+  if (v.stride[3] != 1) return false;
+  if (reinterpret_cast<uintptr_t>(v.data) % 16) return false;
+  for (int i = 0; i < 3; ++i)
+    if ((v.stride[i] * 2) % 16 || v.stride[i] <= 0) return false;
+  return true;
+}
+
+bool tc_fwd_supported(const ts_attn_params& p) {
+  if (p.dtype != TS_BF16 && p.dtype != TS_F16) return false;
+  if (p.head_dim != p.value_dim || (p.head_dim != 64 && p.head_dim != 128)) return false;
+  if (p.mask_kind != TS_MASK_NONE) return false;
+  if (!view_tma_ok(p.q) || !view_tma_ok(p.k) || !view_tma_ok(p.v)) return false;
+  if (p.o.stride[3] != 1 || reinterpret_cast<uintptr_t>(p.o.data) % 16 || (p.o.stride[2] * 2) % 16 ||
+      (p.o.stride[1] * 2) % 16 || (p.o.stride[0] * 2) % 16)
+    return false;
+  return encode_fn() != nullptr;
+}
+
+static bool make_map(CUtensorMap* map, const ts_view4& v, int dtype, int batch, int heads, int len,
+                     int channels) {
+  const cuuint64_t dims[4] = {(cuuint64_t)channels, (cuuint64_t)len, (cuuint64_t)heads, (cuuint64_t)batch};
+  const cuuint64_t strides[3] = {(cuuint64_t)v.stride[2] * 2, (cuuint64_t)v.stride[1] * 2,
+                                 (cuuint64_t)v.stride[0] * 2};
+  const cuuint32_t box[4] = {64, 128, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt =
+      dtype == TS_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return encode_fn()(map, dt, 4, v.data, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int D, bool BF16>
+static cudaError_t launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                             const TcFwdArgs& a, cudaStream_t st) {
+  auto kern = tc_fwd_kernel<D, BF16>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::kSmem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(a.n_q_tiles, a.p.q_heads, a.p.batch);
+  kern<<<grid, 256, Cfg<D>::kSmem, st>>>(mq, mk, mv, a);
+  return cudaGetLastError();
+}
+
+cudaError_t tc_forward(const ts_attn_params& p, uint32_t* fault, cudaStream_t st) {
+  CUtensorMap mq, mk, mv;
+  if (!make_map(&mq, p.q, p.dtype, p.batch, p.q_heads, p.q_len, p.head_dim) ||
+      !make_map(&mk, p.k, p.dtype, p.batch, p.kv_heads, p.kv_len, p.head_dim) ||
+      !make_map(&mv, p.v, p.dtype, p.batch, p.kv_heads, p.kv_len, p.value_dim))
+    return cudaErrorInvalidValue;
+  TcFwdArgs a;
+  a.p = p;
+  a.n_q_tiles = ceil_div(p.q_len, kBM);
+  a.fault = fault;
+  const bool bf = p.dtype == TS_BF16;
+  if (p.head_dim == 64) return bf ? launch_tc<64, true>(mq, mk, mv, a, st) : launch_tc<64, false>(mq, mk, mv, a, st);
+  return bf ? launch_tc<128, true>(mq, mk, mv, a, st) : launch_tc<128, false>(mq, mk, mv, a, st);
+}
+
+}  // namespace tsa

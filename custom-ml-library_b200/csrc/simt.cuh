@@ -1,0 +1,12 @@
+// Entry points of the generic CUDA-core attention kernels (attn_simt.cu).
+#pragma once
+#include "common.cuh"
+
+namespace tsa {
+// Forward O (+ LSE) for any dtype / head dims <= 256 / masks.
+cudaError_t simt_forward(const ts_attn_params& p, cudaStream_t stream);
+// Bytes of workspace simt_backward needs (row deltas in the accumulation type).
+size_t simt_backward_workspace(const ts_attn_bwd_params& bp);
+// dQ, dK, dV from the saved LSE.
+cudaError_t simt_backward(const ts_attn_bwd_params& bp, void* workspace, cudaStream_t stream);
+}  // namespace tsa

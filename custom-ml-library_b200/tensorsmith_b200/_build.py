@@ -1,0 +1,94 @@
+"""Build libts_attn.so in-tree with nvcc for sm_100a.
+
+    python -m tensorsmith_b200._build        (from custom-ml-library_b200/)
+
+Each ``csrc/*.cu`` is compiled to an object in parallel, then linked into
+``tensorsmith_b200/lib/libts_attn.so`` (static CUDA runtime, no driver-library
+link: the tensor-map encoder is fetched with cudaGetDriverEntryPoint).
+"""
+
+from __future__ import annotations
+
+import concurrent.futures
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = ROOT / "csrc"
+BUILD = ROOT / "_build"
+LIB_DIR = PKG / "lib"
+LIB = LIB_DIR / "libts_attn.so"
+INCLUDE = ROOT.parent / "include"
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = [
+    "-O3",
+    "-std=c++17",
+    "-lineinfo",
+    "-Xcompiler",
+    "-fPIC",
+    "-Xcompiler",
+    "-fvisibility=hidden",
+    "--expt-relaxed-constexpr",
+    "-DNDEBUG",
+]
+
+
+def nvcc() -> str:
+    found = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not Path(found).exists():
+        raise RuntimeError("nvcc not found; the B200 engine needs the CUDA toolkit to build")
+    return found
+
+
+def _compile(src: Path, verbose_ptxas: bool) -> tuple[Path, str]:
+    obj = BUILD / (src.stem + ".o")
+    cmd = [nvcc(), *ARCH, *FLAGS, f"-I{INCLUDE}", "-c", str(src), "-o", str(obj)]
+    if verbose_ptxas:
+        cmd += ["-Xptxas", "-v"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed for {src.name}:\n{res.stderr}")
+    return obj, res.stderr
+
+
+def sources() -> list[Path]:
+    return sorted(CSRC.glob("*.cu"))
+
+
+def stale() -> bool:
+    if not LIB.exists():
+        return True
+    built = LIB.stat().st_mtime
+    deps = list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
+    return any(p.stat().st_mtime > built for p in deps)
+
+
+def build(force: bool = False, verbose_ptxas: bool = False, jobs: int | None = None) -> Path:
+    if not force and not stale():
+        return LIB
+    BUILD.mkdir(exist_ok=True)
+    LIB_DIR.mkdir(exist_ok=True)
+    srcs = sources()
+    jobs = jobs or min(len(srcs), os.cpu_count() or 4)
+    with concurrent.futures.ThreadPoolExecutor(jobs) as pool:
+        results = list(pool.map(lambda s: _compile(s, verbose_ptxas), srcs))
+    if verbose_ptxas:
+        for (_, log), src in zip(results, srcs):
+            sys.stderr.write(f"== {src.name}\n{log}")
+    tmp = LIB.with_suffix(".so.tmp")
+    cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *[str(o) for o, _ in results]]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"link failed:\n{res.stderr}")
+    os.replace(tmp, LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    path = build(force="--force" in sys.argv, verbose_ptxas="-v" in sys.argv)
+    print(path)

@@ -1,0 +1,115 @@
+"""Batch x KV-head sharding of the attention path over the GPUs of one node.
+
+Every (batch row, KV head) pair -- with the query heads of its group -- is an
+independent attention problem for prefill, backward and decode, so ranks own
+contiguous blocks of pairs and never reduce.  The only collective is the
+gather of each rank's outputs to the caller's rank (NCCL over NVLink through
+``torch.distributed``).  tensorsmith itself has no such path: its only
+multi-process code is a host-staged TCP all-reduce for data parallelism
+(src/tensorsmith/distributed.py:22-218).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+
+@dataclass(frozen=True)
+class ShardPlan:
+    """Contiguous block of (batch, kv_head) pairs owned by ``rank``."""
+
+    batch: int
+    kv_heads: int
+    world_size: int
+    rank: int
+
+    def __post_init__(self):
+        if self.world_size <= 0 or not 0 <= self.rank < self.world_size:
+            raise ValueError("rank must be in [0, world_size)")
+        if self.batch <= 0 or self.kv_heads <= 0:
+            raise ValueError("batch and kv_heads must be positive")
+
+    @property
+    def pairs(self) -> int:
+        return self.batch * self.kv_heads
+
+    def bounds(self, rank: int | None = None) -> tuple[int, int]:
+        r = self.rank if rank is None else rank
+        return r * self.pairs // self.world_size, (r + 1) * self.pairs // self.world_size
+
+    @property
+    def start(self) -> int:
+        return self.bounds()[0]
+
+    @property
+    def stop(self) -> int:
+        return self.bounds()[1]
+
+    @property
+    def size(self) -> int:
+        return self.stop - self.start
+
+    @property
+    def even(self) -> bool:
+        return self.pairs % self.world_size == 0
+
+    def pair_ids(self) -> list[tuple[int, int]]:
+        return [divmod(i, self.kv_heads) for i in range(self.start, self.stop)]
+
+
+def shard_view(x: torch.Tensor, plan: ShardPlan, group: int = 1) -> torch.Tensor:
+    """This rank's pairs of a [B, H, T, C] tensor, as a view (no copy).
+
+    ``group`` is the number of heads per pair (query heads per KV head for
+    queries/outputs, 1 for keys/values).  When the shard covers whole batch
+    rows the result is ``x[b0:b1]`` (any layout, BTHD-permuted included);
+    otherwise the (B, H) dims are flattened into a [1, pairs*group, T, C] view,
+    which needs them to be flattenable without a copy.
+    """
+    b, h, t, c = x.shape
+    if b != plan.batch or h != plan.kv_heads * group:
+        raise ValueError("tensor does not match the shard plan")
+    if plan.start % plan.kv_heads == 0 and plan.stop % plan.kv_heads == 0:
+        return x[plan.start // plan.kv_heads : plan.stop // plan.kv_heads]
+    if x.stride(0) != h * x.stride(1):
+        raise ValueError("shard splits a batch row of a layout whose (B, H) dims do not flatten")
+    flat = x.as_strided((1, b * h, t, c), (b * h * x.stride(1), x.stride(1), x.stride(2), x.stride(3)))
+    return flat[:, plan.start * group : plan.stop * group]
+
+
+def gather_to_root(local: torch.Tensor, plan: ShardPlan, out: torch.Tensor | None = None,
+                   root: int = 0, group=None):
+    """Gather every rank's shard into ``out`` (the full tensor, same pair order) on ``root``.
+
+    One NCCL gather (grouped send/recv) per call; other ranks return None.
+    Shards must be equal-sized (the plan is even)."""
+    if plan.world_size == 1:
+        if out is not None:
+            out.copy_(local)
+            return out
+        return local
+    if not plan.even:
+        raise ValueError("gather needs an even shard plan (pairs divisible by world size)")
+    rank = dist.get_rank(group)
+    if rank == root:
+        if out is None:
+            shape = list(local.shape)
+            shape[0] *= plan.world_size
+            out = torch.empty(shape, dtype=local.dtype, device=local.device)
+        chunks = list(out.reshape((plan.world_size, -1) + tuple(local.shape[2:])).unbind(0)) \
+            if out.is_contiguous() else None
+        if chunks is None:
+            raise ValueError("gather target must be contiguous")
+        chunks = [c.view(local.shape) for c in chunks]
+        contiguous = all(c.is_contiguous() for c in chunks)
+        targets = chunks if contiguous else [torch.empty_like(local) for _ in chunks]
+        dist.gather(local.contiguous(), targets, dst=root, group=group)
+        if not contiguous:
+            for c, t in zip(chunks, targets):
+                c.copy_(t)
+        return out
+    dist.gather(local.contiguous(), None, dst=root, group=group)
+    return None

@@ -1,0 +1,241 @@
+"""Array-level entry points of the B200 attention engine.
+
+These functions take CUDA device arrays (torch tensors are used as the device
+allocator and stream source; any strided 4-D view is accepted), fill the C-ABI
+parameter structs of include/ts_attn.h and launch on the current stream.  They
+allocate outputs and workspaces on the caller's side of the ABI, exactly as the
+C contract requires, and never compute anything on the host.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+
+_DTYPE_CODES = {
+    torch.float32: _lib.F32,
+    torch.float16: _lib.F16,
+    torch.bfloat16: _lib.BF16,
+    torch.float64: _lib.F64,
+}
+
+# Largest (query heads per KV head) x (query tokens) the split-K decode kernel takes.
+DECODE_MAX_ROWS = 8
+
+
+def lse_dtype(dtype: torch.dtype) -> torch.dtype:
+    """LSE is fp32 (softmax statistics of half/fp32 inputs), fp64 for fp64 inputs."""
+    return torch.float64 if dtype == torch.float64 else torch.float32
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODES[dtype]
+    except KeyError:
+        raise TypeError(f"the B200 attention engine does not support dtype {dtype}") from None
+
+
+def _require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError("the B200 attention engine needs CUDA device tensors")
+
+
+def view4(t: torch.Tensor) -> _lib.View4:
+    if t.dim() != 4:
+        raise ValueError("expected a [batch, heads, sequence, channels] view")
+    return _lib.View4(t.data_ptr(), (ctypes.c_int64 * 4)(*t.stride()))
+
+
+def _stream_handle(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def default_scale(head_dim: int) -> float:
+    """1/sqrt(D), the reference default (nn/attention.py:60)."""
+    return 1.0 / math.sqrt(head_dim)
+
+
+def _mask_args(mask, shape):
+    """Broadcast a bool / float mask to [B, H, Tq, Tk] strides (0 on broadcast axes)."""
+    if mask is None:
+        return _lib.MASK_NONE, None, (0, 0, 0, 0), None
+    if mask.dtype == torch.bool:
+        kind = _lib.MASK_BOOL
+        keep = mask
+    elif mask.is_floating_point():
+        kind = _lib.MASK_ADD_F32
+        keep = mask if mask.dtype == torch.float32 else mask.float()
+    else:
+        raise TypeError("attention masks must be boolean or floating point")
+    try:
+        expanded = keep.expand(*shape)
+    except RuntimeError as error:
+        raise ValueError("attention mask is not broadcastable to [B,H,Q,K]") from error
+    return kind, expanded.data_ptr(), tuple(expanded.stride()), keep
+
+
+def make_params(q, k, v, o, lse, *, is_causal=False, scale=None, causal_offset=0, kv_lens=None,
+                mask=None):
+    """Fill ts_attn_params; returns (params, keepalive) -- keep the tuple alive until launch."""
+    b, hq, tq, d = q.shape
+    hkv, tk, dv = k.shape[1], k.shape[2], v.shape[3]
+    p = _lib.AttnParams()
+    p.q, p.k, p.v, p.o = view4(q), view4(k), view4(v), view4(o)
+    p.lse = lse.data_ptr() if lse is not None else None
+    if lse is not None:
+        p.lse_stride = (ctypes.c_int64 * 3)(*lse.stride())
+    p.dtype = dtype_code(q.dtype)
+    p.batch, p.q_heads, p.kv_heads = b, hq, hkv
+    p.q_len, p.kv_len, p.head_dim, p.value_dim = tq, tk, d, dv
+    p.scale = default_scale(d) if scale is None else float(scale)
+    p.is_causal = 1 if is_causal else 0
+    p.causal_offset = int(causal_offset)
+    lens = None
+    if kv_lens is not None:
+        lens = kv_lens if kv_lens.dtype == torch.int32 else kv_lens.to(torch.int32)
+        p.kv_lens = lens.data_ptr()
+    kind, ptr, strides, keep = _mask_args(mask, (b, hq, tq, tk))
+    p.mask_kind = kind
+    p.mask = ptr
+    p.mask_stride = (ctypes.c_int64 * 4)(*strides)
+    return p, (lens, keep)
+
+
+def _check_inputs(q, k, v):
+    _require_cuda(q, k, v)
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise TypeError("attention inputs must have the same floating-point dtype")
+    dtype_code(q.dtype)
+
+
+def fwd_path(q, k, v, *, decode=False, is_causal=False, scale=None, causal_offset=0, kv_lens=None,
+             mask=None) -> str:
+    """Name of the kernel family the engine selects for this problem."""
+    o = torch.empty((q.shape[0], q.shape[1], q.shape[2], v.shape[3]), dtype=q.dtype, device=q.device)
+    p, keep = make_params(q, k, v, o, None, is_causal=is_causal, scale=scale,
+                          causal_offset=causal_offset, kv_lens=kv_lens, mask=mask)
+    code = _lib.lib().ts_attn_fwd_path(ctypes.byref(p), 1 if decode else 0)
+    if code < 0:
+        _lib.check(code, "ts_attn_fwd_path")
+    return _lib.PATH_NAMES[code]
+
+
+def forward(q, k, v, *, is_causal=False, scale=None, causal_offset=0, kv_lens=None, mask=None,
+            need_lse=True, out=None, lse=None):
+    """Attention forward: returns ``(out [B,Hq,Tq,Dv], lse [B,Hq,Tq] or None)``.
+
+    ``lse`` is fp32 (fp64 for fp64 inputs), natural-log units, -inf on fully masked rows."""
+    _check_inputs(q, k, v)
+    b, hq, tq, _ = q.shape
+    if out is None:
+        out = torch.empty((b, hq, tq, v.shape[3]), dtype=q.dtype, device=q.device)
+    if need_lse and lse is None:
+        lse = torch.empty((b, hq, tq), dtype=lse_dtype(q.dtype), device=q.device)
+    p, keep = make_params(q, k, v, out, lse if need_lse else None, is_causal=is_causal, scale=scale,
+                          causal_offset=causal_offset, kv_lens=kv_lens, mask=mask)
+    _lib.check(_lib.lib().ts_attn_fwd(ctypes.byref(p), _stream_handle(q.device)), "ts_attn_fwd")
+    del keep
+    return out, (lse if need_lse else None)
+
+
+def decode_workspace_bytes(q, k, v, **kw) -> int:
+    o = torch.empty((q.shape[0], q.shape[1], q.shape[2], v.shape[3]), dtype=q.dtype, device=q.device)
+    p, keep = make_params(q, k, v, o, None, **kw)
+    return int(_lib.lib().ts_attn_decode_workspace_size(ctypes.byref(p)))
+
+
+def decode(q, k, v, *, is_causal=True, scale=None, causal_offset=0, kv_lens=None, mask=None,
+           need_lse=False, out=None, lse=None, workspace=None):
+    """Split-K decode for a few query tokens against a long KV cache."""
+    _check_inputs(q, k, v)
+    b, hq, tq, _ = q.shape
+    if out is None:
+        out = torch.empty((b, hq, tq, v.shape[3]), dtype=q.dtype, device=q.device)
+    if need_lse and lse is None:
+        lse = torch.empty((b, hq, tq), dtype=lse_dtype(q.dtype), device=q.device)
+    p, keep = make_params(q, k, v, out, lse if need_lse else None, is_causal=is_causal, scale=scale,
+                          causal_offset=causal_offset, kv_lens=kv_lens, mask=mask)
+    handle = _lib.lib()
+    need = int(handle.ts_attn_decode_workspace_size(ctypes.byref(p)))
+    if need and (workspace is None or workspace.numel() * workspace.element_size() < need):
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    ws_ptr = workspace.data_ptr() if (need and workspace is not None) else None
+    ws_bytes = workspace.numel() * workspace.element_size() if (need and workspace is not None) else 0
+    _lib.check(handle.ts_attn_decode(ctypes.byref(p), ws_ptr, ws_bytes, _stream_handle(q.device)),
+               "ts_attn_decode")
+    del keep
+    return out, (lse if need_lse else None)
+
+
+def backward(q, k, v, out, lse, dout, *, is_causal=False, scale=None, causal_offset=0, kv_lens=None,
+             mask=None, dq=None, dk=None, dv=None):
+    """dQ, dK, dV of attention from the forward output and its LSE."""
+    _check_inputs(q, k, v)
+    _require_cuda(out, lse, dout)
+    dq = torch.empty_like(q) if dq is None else dq
+    dk = torch.empty_like(k) if dk is None else dk
+    dv = torch.empty_like(v) if dv is None else dv
+    if dout.dtype != q.dtype:
+        dout = dout.to(q.dtype)
+    fp, keep = make_params(q, k, v, out, lse, is_causal=is_causal, scale=scale,
+                           causal_offset=causal_offset, kv_lens=kv_lens, mask=mask)
+    bp = _lib.AttnBwdParams()
+    bp.fwd = fp
+    bp.dout, bp.dq, bp.dk, bp.dv = view4(dout), view4(dq), view4(dk), view4(dv)
+    handle = _lib.lib()
+    need = int(handle.ts_attn_bwd_workspace_size(ctypes.byref(bp)))
+    ws = torch.empty(max(need, 16), dtype=torch.uint8, device=q.device)
+    _lib.check(handle.ts_attn_bwd(ctypes.byref(bp), ws.data_ptr(), ws.numel(), _stream_handle(q.device)),
+               "ts_attn_bwd")
+    del keep
+    return dq, dk, dv
+
+
+def kv_append(key, value, key_cache, value_cache, *, position=0, positions=None, positions_out=None):
+    """Write a [B,H,steps,C] chunk into [B,H,cap,C] caches at ``position`` (or per-row ``positions``)."""
+    _require_cuda(key, value, key_cache, value_cache)
+    p = _lib.KvAppendParams()
+    p.key, p.value = view4(key), view4(value)
+    p.key_cache, p.value_cache = view4(key_cache), view4(value_cache)
+    p.src_dtype = dtype_code(key.dtype)
+    p.cache_dtype = dtype_code(key_cache.dtype)
+    if value.dtype != key.dtype or value_cache.dtype != key_cache.dtype:
+        raise TypeError("key/value and their caches must share a dtype each")
+    p.batch, p.heads, p.steps = key.shape[0], key.shape[1], key.shape[2]
+    p.head_dim, p.value_dim, p.capacity = key.shape[3], value.shape[3], key_cache.shape[2]
+    p.position = int(position)
+    p.positions = positions.data_ptr() if positions is not None else None
+    p.positions_out = positions_out.data_ptr() if positions_out is not None else None
+    _lib.check(_lib.lib().ts_kv_append(ctypes.byref(p), _stream_handle(key.device)), "ts_kv_append")
+
+
+def kv_reorder(src, dst, index, length):
+    """dst[b, :, :length] = src[index[b], :, :length] (beam reorder)."""
+    _require_cuda(src, dst, index)
+    idx = index if index.dtype == torch.int32 else index.to(torch.int32)
+    _lib.check(
+        _lib.lib().ts_kv_reorder(view4(src), view4(dst), dtype_code(src.dtype), src.shape[0],
+                                 src.shape[1], int(length), src.shape[3], idx.data_ptr(),
+                                 _stream_handle(src.device)),
+        "ts_kv_reorder",
+    )
+
+
+def device_status(device=None) -> tuple[int, int]:
+    """(status, site) of the device fault word; clears it.  Synchronises the stream."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    info = ctypes.c_uint32(0)
+    with torch.cuda.device(device):
+        status = _lib.lib().ts_attn_device_status(_stream_handle(device), ctypes.byref(info))
+    return status, info.value
+
+
+def check_device_status(device=None) -> None:
+    status, site = device_status(device)
+    if status != _lib.OK:
+        raise _lib.EngineError(status, f"device fault site 0x{site:x}")

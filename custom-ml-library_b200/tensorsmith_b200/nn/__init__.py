@@ -1,0 +1,4 @@
+"""tensorsmith ``nn`` attention surface served by the B200 engine."""
+
+from .attention import scaled_dot_product_attention  # noqa: F401
+from .cache import KVCache  # noqa: F401

@@ -1,0 +1,176 @@
+"""``KVCache`` with tensorsmith's API, stored in HBM and written by the engine.
+
+Constructor arguments, ``append``/``get``/``reset``/``truncate``/``reorder``/
+``storage``/``memory_bytes``/``length`` and their validation follow
+src/tensorsmith/nn/cache.py:12-142.  Storage is ``[B, H, capacity, D]`` per
+tensor (the reference layout), zero-initialised, so a decode kernel may read a
+whole 128-key tile past a row's valid length without meeting non-finite
+values.
+
+Engine extension for ragged batches (the reference expresses them with a
+key-valid mask over a padded cache, docs/transformers.md:52-55): after
+``set_lengths(lengths)`` every row has its own valid length; ``append``
+then writes each row at its own position and ``seq_lens`` is the device
+int32 vector to pass as ``kv_lens`` to ``scaled_dot_product_attention``.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from .. import engine
+from ..tensor import Tensor, as_device, is_grad_enabled
+
+_DTYPES = {
+    "float32": torch.float32,
+    "float16": torch.float16,
+    "bfloat16": torch.bfloat16,
+    "float64": torch.float64,
+}
+
+
+def _torch_dtype(dtype) -> torch.dtype:
+    if isinstance(dtype, torch.dtype):
+        return dtype
+    name = str(dtype).replace("torch.", "")
+    if name in _DTYPES:
+        return _DTYPES[name]
+    try:
+        return _DTYPES[np.dtype(dtype).name]
+    except (TypeError, KeyError):
+        raise TypeError("cache compute dtype must be floating point") from None
+
+
+class KVCache:
+    """Preallocated [B,H,capacity,D] keys/values for autoregressive inference."""
+
+    def __init__(self, batch_size: int, num_heads: int, head_dim: int, max_seq_len: int, *,
+                 device="cuda", dtype="float32", quantized: bool = False, value_dim=None):
+        if min(batch_size, num_heads, head_dim, max_seq_len) <= 0:
+            raise ValueError("cache dimensions and capacity must be positive")
+        self.batch_size, self.num_heads, self.head_dim = batch_size, num_heads, head_dim
+        self.value_dim = head_dim if value_dim is None else value_dim
+        if self.value_dim <= 0:
+            raise ValueError("value_dim must be positive")
+        self.max_seq_len = max_seq_len
+        self.device = as_device(device)
+        if self.device.type != "cuda":
+            raise ValueError("the B200 KV cache lives on a cuda device")
+        self.dtype = _torch_dtype(dtype)
+        if not self.dtype.is_floating_point:
+            raise TypeError("cache compute dtype must be floating point")
+        if quantized:
+            raise NotImplementedError("int8 KV storage is not implemented by the B200 engine")
+        self.quantized = False
+        self.length = 0
+        dev = torch.device("cuda", self.device.index)
+        shape = (batch_size, num_heads, max_seq_len)
+        self._keys = torch.zeros(shape + (head_dim,), dtype=self.dtype, device=dev)
+        self._values = torch.zeros(shape + (self.value_dim,), dtype=self.dtype, device=dev)
+        self._host_lens: np.ndarray | None = None
+        self._lens: torch.Tensor | None = None
+        self._lens_next: torch.Tensor | None = None
+
+    # -- reference API -----------------------------------------------------
+    def append(self, key: Tensor, value: Tensor) -> tuple[Tensor, Tensor]:
+        """Append a chunk after validating all shapes and capacity."""
+        if key.device != self.device or value.device != self.device:
+            raise ValueError("cache and key/value tensors must be on the same device")
+        if is_grad_enabled() and (key.requires_grad or value.requires_grad):
+            raise RuntimeError("KVCache is inference-only; use no_grad() for differentiable inputs")
+        prefix = (self.batch_size, self.num_heads)
+        if key.ndim != 4 or key.shape[:2] != prefix or key.shape[-1] != self.head_dim:
+            raise ValueError("key shape does not match cache configuration")
+        if value.shape != key.shape[:3] + (self.value_dim,):
+            raise ValueError("value shape does not match cache configuration")
+        steps = key.shape[2]
+        top = self.length if self._host_lens is None else int(self._host_lens.max())
+        stop = top + steps
+        if steps == 0 or stop > self.max_seq_len:
+            raise ValueError(f"cache capacity {self.max_seq_len} exceeded or empty append")
+        if self._host_lens is None:
+            engine.kv_append(key._data, value._data, self._keys, self._values, position=self.length)
+            self.length = stop
+        else:
+            engine.kv_append(key._data, value._data, self._keys, self._values, positions=self._lens,
+                             positions_out=self._lens_next)
+            self._lens, self._lens_next = self._lens_next, self._lens
+            self._host_lens = self._host_lens + steps
+            self.length = int(self._host_lens.max())
+        return self.get()
+
+    def get(self) -> tuple[Tensor, Tensor]:
+        keys = self._keys[:, :, : self.length]
+        values = self._values[:, :, : self.length]
+        return Tensor(keys, device=self.device), Tensor(values, device=self.device)
+
+    def reset(self) -> None:
+        """Reuse the allocation; future appends overwrite old entries."""
+        self.length = 0
+        if self._host_lens is not None:
+            self.set_lengths(np.zeros(self.batch_size, dtype=np.int64))
+
+    def truncate(self, length: int) -> None:
+        if not 0 <= length <= self.length:
+            raise ValueError("truncate length must be between zero and the current length")
+        self.length = length
+        if self._host_lens is not None:
+            self.set_lengths(np.minimum(self._host_lens, length))
+
+    def reorder(self, indices) -> None:
+        """Reorder or duplicate batch rows for fixed-width beam search (device gather)."""
+        raw = indices._data if isinstance(indices, Tensor) else indices
+        host = raw.detach().cpu().numpy() if isinstance(raw, torch.Tensor) else np.asarray(raw)
+        if host.shape != (self.batch_size,) or host.dtype.kind not in "iu":
+            raise ValueError("beam indices must be one integer per cache batch row")
+        if (host < 0).any() or (host >= self.batch_size).any():
+            raise ValueError("beam index out of range")
+        dev = self._keys.device
+        order = torch.as_tensor(host.astype(np.int32), device=dev)
+        keys, values = torch.empty_like(self._keys), torch.empty_like(self._values)
+        engine.kv_reorder(self._keys, keys, order, self.max_seq_len)
+        engine.kv_reorder(self._values, values, order, self.max_seq_len)
+        self._keys, self._values = keys, values
+        if self._host_lens is not None:
+            self.set_lengths(self._host_lens[host])
+
+    @property
+    def storage(self) -> tuple:
+        """Raw persistent arrays (keys, values, key scales, value scales)."""
+        return self._keys, self._values, None, None
+
+    @property
+    def memory_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self._keys, self._values))
+
+    def __len__(self):
+        return self.length
+
+    def __repr__(self):
+        return (f"KVCache(length={self.length}, capacity={self.max_seq_len}, "
+                f"quantized={self.quantized}, device='{self.device}')")
+
+    # -- ragged rows (engine extension) ------------------------------------
+    def set_lengths(self, lengths) -> None:
+        """Give every batch row its own valid length (keys beyond it are ignored)."""
+        host = np.asarray(lengths, dtype=np.int64).reshape(-1)
+        if host.shape != (self.batch_size,) or (host < 0).any() or (host > self.max_seq_len).any():
+            raise ValueError("lengths must be one value in [0, capacity] per cache batch row")
+        dev = self._keys.device
+        self._host_lens = host.copy()
+        self._lens = torch.as_tensor(host.astype(np.int32), device=dev)
+        self._lens_next = torch.empty_like(self._lens)
+        self.length = int(host.max()) if host.size else 0
+
+    @property
+    def lengths(self) -> np.ndarray:
+        """Per-row valid lengths (host copy)."""
+        if self._host_lens is None:
+            return np.full(self.batch_size, self.length, dtype=np.int64)
+        return self._host_lens.copy()
+
+    @property
+    def seq_lens(self) -> torch.Tensor | None:
+        """Device int32 [B] per-row lengths, or None when every row has ``length`` keys."""
+        return self._lens

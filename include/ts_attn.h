@@ -1,0 +1,167 @@
+/*
+ * ts_attn.h -- C ABI of the B200 attention engine for tensorsmith.
+ *
+ * The engine replaces the compute behind tensorsmith's attention path
+ * (tensorsmith 0.3.0; file:line below are relative to the tensorsmith project
+ * root).  Every entry point takes plain device pointers, element strides and
+ * sizes; the caller owns all memory (outputs and workspaces included).  Calls
+ * are asynchronous on the given CUDA stream (a cudaStream_t passed as void*,
+ * NULL = legacy default stream) of the current device.  Every entry point
+ * returns TS_OK (0) or a negative ts_status and never aborts the process.
+ *
+ * Layout convention: a 4-D view [batch, heads, sequence, channels] is a base
+ * pointer plus four ELEMENT strides, so tensors coming from tensorsmith's
+ * reshape/permute (nn/transformer.py:124-138, memory order B,T,H,D) are
+ * accepted without a copy.
+ */
+#ifndef TS_ATTN_H
+#define TS_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TS_ATTN_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define TS_ATTN_API __attribute__((visibility("default")))
+#else
+#define TS_ATTN_API
+#endif
+
+/* Element types.  Half types compute in fp32 with fp32 softmax statistics,
+ * as the reference does (nn/attention.py:63); fp64 computes in fp64. */
+typedef enum ts_dtype { TS_F32 = 0, TS_F16 = 1, TS_BF16 = 2, TS_F64 = 3 } ts_dtype;
+
+/* Optional attention mask of nn/attention.py:64-76, 105-107:
+ * BOOL  -- uint8 0/1, True (1) = allowed, False -> score -inf;
+ * ADD   -- fp32 values added to the scaled scores. */
+typedef enum ts_mask_kind { TS_MASK_NONE = 0, TS_MASK_BOOL = 1, TS_MASK_ADD_F32 = 2 } ts_mask_kind;
+
+typedef enum ts_status {
+  TS_OK = 0,
+  TS_ERR_INVALID_ARGUMENT = -1, /* shape / stride / pointer / value check failed */
+  TS_ERR_UNSUPPORTED = -2,      /* combination not implemented by any kernel */
+  TS_ERR_WORKSPACE = -3,        /* workspace missing or smaller than required */
+  TS_ERR_LAUNCH = -4,           /* kernel launch or driver call failed */
+  TS_ERR_DEVICE_TIMEOUT = -5,   /* a bounded wait inside a kernel gave up */
+  TS_ERR_CAPACITY = -6          /* KV-cache append would exceed the capacity */
+} ts_status;
+
+/* Which kernel family ts_attn_fwd would run (for tests and diagnostics). */
+typedef enum ts_fwd_path {
+  TS_PATH_NONE = 0,
+  TS_PATH_TCGEN05 = 1, /* bf16/f16 tensor-core prefill (tcgen05 + TMEM + TMA) */
+  TS_PATH_SIMT = 2,    /* generic CUDA-core path (any dtype/dim/mask) */
+  TS_PATH_DECODE = 3   /* split-K HBM-streaming decode */
+} ts_fwd_path;
+
+/* A [B, H, T, C] view: base pointer + element strides (b, h, t, c). */
+typedef struct ts_view4 {
+  void* data;
+  int64_t stride[4];
+} ts_view4;
+
+/* Forward / decode problem.  Mirrors the arguments of
+ * scaled_dot_product_attention (nn/attention.py:16-29). */
+typedef struct ts_attn_params {
+  ts_view4 q;  /* [B, Hq,  Tq, D]  */
+  ts_view4 k;  /* [B, Hkv, Tk, D]  */
+  ts_view4 v;  /* [B, Hkv, Tk, Dv] */
+  ts_view4 o;  /* [B, Hq,  Tq, Dv] output, same dtype as q */
+  /* optional [B, Hq, Tq] natural-log normaliser (-inf = fully masked row);
+   * fp32, or fp64 when dtype is TS_F64 */
+  void* lse;
+  int64_t lse_stride[3];
+  int32_t dtype; /* ts_dtype of q, k, v and o */
+  int32_t batch, q_heads, kv_heads, q_len, kv_len, head_dim, value_dim;
+  float scale;           /* softmax scale; the reference default is 1/sqrt(D) (nn/attention.py:60) */
+  int32_t is_causal;     /* key j visible to query i iff i + offset >= j (nn/attention.py:108-111) */
+  int64_t causal_offset; /* absolute position of query 0 in the key sequence */
+  /* Optional per-row valid key count [B] (int32, device).  Keys j >= kv_lens[b]
+   * are masked.  When set together with is_causal, the queries of row b sit at
+   * the end of its valid keys: offset_b = kv_lens[b] - q_len (causal_offset is
+   * then ignored).  Expresses tensorsmith's padded-cache + key-valid-mask idiom
+   * (docs/transformers.md:52-55) without a mask tensor. */
+  const int32_t* kv_lens;
+  int32_t mask_kind;  /* ts_mask_kind */
+  const void* mask;   /* [B, Hq, Tq, Tk] with broadcast (0) strides allowed */
+  int64_t mask_stride[4];
+} ts_attn_params;
+
+/* Backward problem: the forward problem plus upstream and gradient views. */
+typedef struct ts_attn_bwd_params {
+  ts_attn_params fwd; /* q, k, v, o (forward output) and lse (required) */
+  ts_view4 dout;      /* [B, Hq,  Tq, Dv] upstream gradient, dtype of q */
+  ts_view4 dq;        /* [B, Hq,  Tq, D]  */
+  ts_view4 dk;        /* [B, Hkv, Tk, D]  (summed over the query-head group) */
+  ts_view4 dv;        /* [B, Hkv, Tk, Dv] */
+} ts_attn_bwd_params;
+
+/* KV-cache append: write a [B, H, steps, C] chunk at positions
+ * [pos_b, pos_b + steps) of [B, H, capacity, C] caches. */
+typedef struct ts_kv_append_params {
+  ts_view4 key, value;             /* new chunk */
+  ts_view4 key_cache, value_cache; /* preallocated storage */
+  int32_t src_dtype;               /* ts_dtype of key/value (cast on write) */
+  int32_t cache_dtype;             /* ts_dtype of the caches */
+  int32_t batch, heads, steps, head_dim, value_dim, capacity;
+  int64_t position;          /* write offset for every row when positions == NULL */
+  const int32_t* positions;  /* optional [B] per-row write offsets (device) */
+  int32_t* positions_out;    /* optional [B]: receives positions[b] + steps */
+} ts_kv_append_params;
+
+/* ABI version (TS_ATTN_ABI_VERSION) of the loaded library. */
+TS_ATTN_API int ts_attn_abi_version(void);
+
+/* Static description of a status code. */
+TS_ATTN_API const char* ts_attn_strerror(int status);
+
+/* Kernel family ts_attn_fwd / ts_attn_decode would select (ts_fwd_path), or a
+ * negative ts_status when the parameters are invalid. */
+TS_ATTN_API int ts_attn_fwd_path(const ts_attn_params* params, int decode);
+
+/* Prefill / training forward: O and (optionally) LSE.  Replaces the dense,
+ * streaming and native forwards of nn/attention.py:132-198 (the native slot
+ * :146-174 is where tensorsmith plugs a vendor kernel). */
+TS_ATTN_API int ts_attn_fwd(const ts_attn_params* params, void* stream);
+
+/* Workspace bytes ts_attn_bwd needs (fp32 row statistics). */
+TS_ATTN_API size_t ts_attn_bwd_workspace_size(const ts_attn_bwd_params* params);
+
+/* Backward: dQ, dK, dV from recomputed probabilities (LSE of the forward).
+ * Replaces the dense / blockwise VJP and the GQA reduction of
+ * nn/attention.py:200-248. */
+TS_ATTN_API int ts_attn_bwd(const ts_attn_bwd_params* params, void* workspace, size_t workspace_bytes,
+                void* stream);
+
+/* Workspace bytes ts_attn_decode needs (per-split partial results). */
+TS_ATTN_API size_t ts_attn_decode_workspace_size(const ts_attn_params* params);
+
+/* Cached decode: a few query tokens against a long KV cache, split along the
+ * keys and combined.  Same semantics as ts_attn_fwd; replaces the cached call
+ * of nn/transformer.py:144-154 into nn/attention.py:132-145. */
+TS_ATTN_API int ts_attn_decode(const ts_attn_params* params, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/* KVCache.append slice write (nn/cache.py:54-86, unquantized storage). */
+TS_ATTN_API int ts_kv_append(const ts_kv_append_params* params, void* stream);
+
+/* KVCache.reorder batch gather (nn/cache.py:110-123): dst[b] = src[index[b]].
+ * src and dst must not overlap. */
+TS_ATTN_API int ts_kv_reorder(ts_view4 src, ts_view4 dst, int32_t dtype, int32_t batch, int32_t heads,
+                  int32_t length, int32_t channels, const int32_t* index, void* stream);
+
+/* Reads and clears the device fault word written by kernels whose bounded
+ * waits gave up.  Synchronises `stream`.  Returns TS_OK or
+ * TS_ERR_DEVICE_TIMEOUT; *info (optional) receives the recorded site code. */
+TS_ATTN_API int ts_attn_device_status(void* stream, uint32_t* info);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TS_ATTN_H */

@@ -1,0 +1,67 @@
+"""Backward parity: engine dQ/dK/dV (through the C ABI) vs the oracle's VJP
+(LSE-recomputed blockwise VJP of nn/attention.py:220-247, GQA-reduced)."""
+
+import numpy as np
+import pytest
+
+from helpers import assert_close, oracle_backward, rounded, to_cuda, to_np
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+from tensorsmith_b200 import engine  # noqa: E402
+
+SHAPES = [
+    (1, 2, 2, 3, 5, 4, 3, True, 2),
+    (1, 4, 2, 3, 5, 4, 4, False, 0),
+    (1, 2, 2, 7, 7, 8, 8, True, 0),
+    (2, 4, 4, 256, 256, 64, 64, True, 0),
+    (1, 2, 1, 65, 127, 32, 48, True, 62),
+    (1, 2, 2, 130, 130, 128, 128, True, 0),
+]
+
+
+def _case(shape, name, seed):
+    b, hq, hkv, tq, tk, d, dv, causal, off = shape
+    rng = np.random.default_rng(seed)
+    q = rounded(rng.standard_normal((b, hq, tq, d)), name)
+    k = rounded(rng.standard_normal((b, hkv, tk, d)), name)
+    v = rounded(rng.standard_normal((b, hkv, tk, dv)), name)
+    g = rounded(rng.standard_normal((b, hq, tq, dv)), name)
+    return q, k, v, g
+
+
+@pytest.mark.parametrize("name", ["float32", "float64", "float16", "bfloat16"])
+@pytest.mark.parametrize("shape", SHAPES, ids=str)
+def test_backward(shape, name):
+    b, hq, hkv, tq, tk, d, dv, causal, off = shape
+    q, k, v, g = _case(shape, name, 3)
+    kw = dict(is_causal=causal, causal_offset=off, enable_gqa=hq != hkv)
+    _, _, (rdq, rdk, rdv) = oracle_backward(q, k, v, g, **kw)
+    tq_, tk_, tv_, tg = (to_cuda(x, name) for x in (q, k, v, g))
+    out, lse = engine.forward(tq_, tk_, tv_, is_causal=causal, causal_offset=off)
+    dq, dk, dv_ = engine.backward(tq_, tk_, tv_, out, lse, tg, is_causal=causal, causal_offset=off)
+    torch.cuda.synchronize()
+    engine.check_device_status()
+    assert_close(to_np(dq), rdq, name, f"dq {shape}")
+    assert_close(to_np(dk), rdk, name, f"dk {shape}")
+    assert_close(to_np(dv_), rdv, name, f"dv {shape}")
+
+
+@pytest.mark.parametrize("kind", ["bool", "float"])
+def test_backward_masked_rows_have_zero_grad(kind):
+    rng = np.random.default_rng(11)
+    q, k, v, g = (rng.standard_normal((2, 2, 4, 4)).astype(np.float32) for _ in range(4))
+    boolean = np.ones((4, 4), dtype=bool)
+    boolean[1] = False
+    boolean[3, 0] = False
+    mask = boolean if kind == "bool" else np.where(boolean, 0, -np.inf).astype(np.float32)
+    _, _, (rdq, rdk, rdv) = oracle_backward(q, k, v, g, mask=mask, is_causal=True)
+    tm = torch.from_numpy(mask).cuda()
+    tq_, tk_, tv_, tg = (to_cuda(x, "float32") for x in (q, k, v, g))
+    out, lse = engine.forward(tq_, tk_, tv_, is_causal=True, mask=tm)
+    dq, dk, dv_ = engine.backward(tq_, tk_, tv_, out, lse, tg, is_causal=True, mask=tm)
+    assert_close(to_np(dq), rdq, "float32", "dq")
+    assert_close(to_np(dk), rdk, "float32", "dk")
+    assert_close(to_np(dv_), rdv, "float32", "dv")
+    assert np.all(to_np(dq)[:, :, 1] == 0)
