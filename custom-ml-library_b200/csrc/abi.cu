@@ -45,7 +45,7 @@ int check_params(const ts_attn_params* p) {
   if (p->head_dim > 256 || p->value_dim > 256) return TS_ERR_UNSUPPORTED;
   if (!p->q.data || !p->k.data || !p->v.data || !p->o.data) return TS_ERR_INVALID_ARGUMENT;
   if (p->causal_offset < 0) return TS_ERR_INVALID_ARGUMENT;
-  if (!(p->scale == p->scale) || p->scale > 3.0e38f || p->scale < -3.0e38f) return TS_ERR_INVALID_ARGUMENT;
+  if (!(p->scale == p->scale) || p->scale > 1.0e300 || p->scale < -1.0e300) return TS_ERR_INVALID_ARGUMENT;
   if (p->mask_kind < TS_MASK_NONE || p->mask_kind > TS_MASK_ADD_F32) return TS_ERR_INVALID_ARGUMENT;
   if (p->mask_kind != TS_MASK_NONE && !p->mask) return TS_ERR_INVALID_ARGUMENT;
   return TS_OK;

@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(256, 1)
     const int row = (warp - 4) * 32 + lane;
     const int qi = q0 + row;
     const uint32_t t_row = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    const float qk_scale = p.scale * kLog2e;
+    const float qk_scale = (float)p.scale * kLog2e;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = !dead;
     for (int j = 0; j < n_tiles && ok; ++j) {

@@ -48,7 +48,7 @@ __device__ __forceinline__ bool mask_apply(const ts_attn_params& p, int b, int h
   const int64_t idx = (int64_t)b * p.mask_stride[0] + (int64_t)h * p.mask_stride[1] +
                       (int64_t)i * p.mask_stride[2] + (int64_t)j * p.mask_stride[3];
   if (p.mask_kind == TS_MASK_BOOL) return reinterpret_cast<const uint8_t*>(p.mask)[idx] != 0;
-  s += (A)reinterpret_cast<const float*>(p.mask)[idx];
+  s += reinterpret_cast<const A*>(p.mask)[idx];
   return true;
 }
 

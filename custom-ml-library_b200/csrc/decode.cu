@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(DecodeLaunch 
   // ------------------------------- compute --------------------------------
   const int sub = lane / kLanesPerRow;        // row slot of this lane within a warp step
   const int cvec = lane % kLanesPerRow;       // 16-byte vector index within the row
-  const float qscale = p.scale * kLog2e;
+  const float qscale = (float)p.scale * kLog2e;
   float q[NQ][kVec];
 #pragma unroll
   for (int n = 0; n < NQ; ++n) {

@@ -52,7 +52,7 @@ class AttnParams(ctypes.Structure):
         ("kv_len", ctypes.c_int32),
         ("head_dim", ctypes.c_int32),
         ("value_dim", ctypes.c_int32),
-        ("scale", ctypes.c_float),
+        ("scale", ctypes.c_double),
         ("is_causal", ctypes.c_int32),
         ("causal_offset", ctypes.c_int64),
         ("kv_lens", ctypes.c_void_p),

@@ -60,8 +60,10 @@ def default_scale(head_dim: int) -> float:
     return 1.0 / math.sqrt(head_dim)
 
 
-def _mask_args(mask, shape):
-    """Broadcast a bool / float mask to [B, H, Tq, Tk] strides (0 on broadcast axes)."""
+def _mask_args(mask, shape, dtype):
+    """Broadcast a bool / float mask to [B, H, Tq, Tk] strides (0 on broadcast axes).
+
+    Additive masks are passed in the accumulation type (fp64 for fp64 inputs, else fp32)."""
     if mask is None:
         return _lib.MASK_NONE, None, (0, 0, 0, 0), None
     if mask.dtype == torch.bool:
@@ -69,7 +71,8 @@ def _mask_args(mask, shape):
         keep = mask
     elif mask.is_floating_point():
         kind = _lib.MASK_ADD_F32
-        keep = mask if mask.dtype == torch.float32 else mask.float()
+        acc = lse_dtype(dtype)
+        keep = mask if mask.dtype == acc else mask.to(acc)
     else:
         raise TypeError("attention masks must be boolean or floating point")
     try:
@@ -99,7 +102,7 @@ def make_params(q, k, v, o, lse, *, is_causal=False, scale=None, causal_offset=0
     if kv_lens is not None:
         lens = kv_lens if kv_lens.dtype == torch.int32 else kv_lens.to(torch.int32)
         p.kv_lens = lens.data_ptr()
-    kind, ptr, strides, keep = _mask_args(mask, (b, hq, tq, tk))
+    kind, ptr, strides, keep = _mask_args(mask, (b, hq, tq, tk), q.dtype)
     p.mask_kind = kind
     p.mask = ptr
     p.mask_stride = (ctypes.c_int64 * 4)(*strides)

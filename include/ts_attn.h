@@ -38,7 +38,7 @@ typedef enum ts_dtype { TS_F32 = 0, TS_F16 = 1, TS_BF16 = 2, TS_F64 = 3 } ts_dty
 
 /* Optional attention mask of nn/attention.py:64-76, 105-107:
  * BOOL  -- uint8 0/1, True (1) = allowed, False -> score -inf;
- * ADD   -- fp32 values added to the scaled scores. */
+ * ADD   -- values added to the scaled scores: fp32, or fp64 when dtype is TS_F64. */
 typedef enum ts_mask_kind { TS_MASK_NONE = 0, TS_MASK_BOOL = 1, TS_MASK_ADD_F32 = 2 } ts_mask_kind;
 
 typedef enum ts_status {
@@ -78,7 +78,7 @@ typedef struct ts_attn_params {
   int64_t lse_stride[3];
   int32_t dtype; /* ts_dtype of q, k, v and o */
   int32_t batch, q_heads, kv_heads, q_len, kv_len, head_dim, value_dim;
-  float scale;           /* softmax scale; the reference default is 1/sqrt(D) (nn/attention.py:60) */
+  double scale;          /* softmax scale; the reference default is 1/sqrt(D) (nn/attention.py:60) */
   int32_t is_causal;     /* key j visible to query i iff i + offset >= j (nn/attention.py:108-111) */
   int64_t causal_offset; /* absolute position of query 0 in the key sequence */
   /* Optional per-row valid key count [B] (int32, device).  Keys j >= kv_lens[b]
