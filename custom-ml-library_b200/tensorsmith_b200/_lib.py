@@ -31,6 +31,9 @@ ERR_LAUNCH = -4
 ERR_DEVICE_TIMEOUT = -5
 ERR_CAPACITY = -6
 
+# Fixed device scratch of ts_attn_decode_noalloc (TS_ATTN_NOALLOC_SCRATCH_BYTES).
+NOALLOC_SCRATCH_BYTES = 8 << 20
+
 
 class View4(ctypes.Structure):
     _fields_ = [("data", ctypes.c_void_p), ("stride", ctypes.c_int64 * 4)]
@@ -102,6 +105,7 @@ SIGNATURES = {
         ctypes.c_int,
         [ctypes.POINTER(AttnParams), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p],
     ),
+    "ts_attn_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(AttnParams), ctypes.c_void_p]),
     "ts_kv_append": (ctypes.c_int, [ctypes.POINTER(KvAppendParams), ctypes.c_void_p]),
     "ts_kv_reorder": (
         ctypes.c_int,

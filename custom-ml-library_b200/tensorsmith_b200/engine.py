@@ -175,6 +175,32 @@ def decode(q, k, v, *, is_causal=True, scale=None, causal_offset=0, kv_lens=None
     return out, (lse if need_lse else None)
 
 
+def decode_noalloc(q, k, v, *, is_causal=True, scale=None, causal_offset=0, kv_lens=None,
+                   need_lse=False, out=None, lse=None):
+    """Decode through ts_attn_decode_noalloc: no workspace, no device allocation by the engine.
+
+    For callers that cannot allocate device memory at decode time (all HBM
+    already handed to KV-cache pages, or no cudaMalloc allowed between decode
+    steps).  The split partials go to the library's fixed 8 MiB per-device
+    scratch; calls that overlap on one device race on it.  Pass ``out`` (and
+    ``lse`` when ``need_lse``) preallocated to keep the call allocation-free."""
+    _check_inputs(q, k, v)
+    b, hq, tq, _ = q.shape
+    if out is None:
+        out = torch.empty((b, hq, tq, v.shape[3]), dtype=q.dtype, device=q.device)
+    if need_lse and lse is None:
+        lse = torch.empty((b, hq, tq), dtype=lse_dtype(q.dtype), device=q.device)
+    p, keep = make_params(q, k, v, out, lse if need_lse else None, is_causal=is_causal, scale=scale,
+                          causal_offset=causal_offset, kv_lens=kv_lens)
+    status = _lib.lib().ts_attn_decode_noalloc(ctypes.byref(p), _stream_handle(q.device))
+    if status == _lib.ERR_WORKSPACE:
+        raise _lib.EngineError(status, "ts_attn_decode_noalloc: problem needs more than the fixed "
+                               f"{_lib.NOALLOC_SCRATCH_BYTES >> 20} MiB decode scratch")
+    _lib.check(status, "ts_attn_decode_noalloc")
+    del keep
+    return out, (lse if need_lse else None)
+
+
 def backward(q, k, v, out, lse, dout, *, is_causal=False, scale=None, causal_offset=0, kv_lens=None,
              mask=None, dq=None, dk=None, dv=None):
     """dQ, dK, dV of attention from the forward output and its LSE."""

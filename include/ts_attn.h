@@ -155,6 +155,21 @@ TS_ATTN_API int ts_kv_append(const ts_kv_append_params* params, void* stream);
 TS_ATTN_API int ts_kv_reorder(ts_view4 src, ts_view4 dst, int32_t dtype, int32_t batch, int32_t heads,
                   int32_t length, int32_t channels, const int32_t* index, void* stream);
 
+/* Size of the fixed device scratch ts_attn_decode_noalloc uses (8 MiB per GPU). */
+#define TS_ATTN_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
+
+/* Decode for callers that cannot allocate device memory (no counterpart in
+ * tensorsmith): e.g. a serving loop whose allocator already gave all free HBM
+ * to KV-cache pages, or host code that must not call cudaMalloc (which may
+ * synchronise the device) between decode steps.  Same semantics and kernels as
+ * ts_attn_decode, but the split partials live in a fixed library-owned device
+ * array of TS_ATTN_NOALLOC_SCRATCH_BYTES on every GPU that loads the library,
+ * held until exit.  The first call on a device looks up the array's device
+ * address (make it before any stream capture); calls that overlap on the GPU
+ * share the array and race.  Returns TS_ERR_WORKSPACE, launching nothing, when
+ * the problem needs more scratch than that.  Allocates nothing. */
+TS_ATTN_API int ts_attn_decode_noalloc(const ts_attn_params* params, void* stream);
+
 /* Reads and clears the device fault word written by kernels whose bounded
  * waits gave up.  Synchronises `stream`.  Returns TS_OK or
  * TS_ERR_DEVICE_TIMEOUT; *info (optional) receives the recorded site code. */

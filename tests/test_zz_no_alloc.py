@@ -1,0 +1,69 @@
+"""ts_attn_decode_noalloc: the decode entry point for callers that cannot
+allocate device memory (for example a serving loop that gave all free HBM to
+its KV cache, or one that must not call cudaMalloc between decode steps).
+
+It is called through the C ABI and compared with ts_attn_decode (which takes a
+caller-allocated workspace) within the tests' fp16/bf16 tolerance, on two calls
+in a row: the second call reuses the fixed scratch the first one left behind.
+This file is collected last so a failure here never hides the other tests."""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from helpers import HALF_MAXABS
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+from tensorsmith_b200 import _lib, engine  # noqa: E402
+
+
+def _problem(seed, b, hq, hkv, cap, lens):
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    q = torch.randn(b, hq, 1, 128, generator=gen, device="cuda").to(torch.bfloat16)
+    k = torch.randn(b, hkv, cap, 128, generator=gen, device="cuda").to(torch.bfloat16)
+    v = torch.randn(b, hkv, cap, 128, generator=gen, device="cuda").to(torch.bfloat16)
+    kv_lens = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    return q, k, v, kv_lens
+
+
+def _noalloc(q, k, v, kv_lens):
+    out = torch.empty_like(q)
+    lse = torch.empty(q.shape[:3], dtype=torch.float32, device="cuda")
+    params, keep = engine.make_params(q, k, v, out, lse, is_causal=True, kv_lens=kv_lens)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    status = _lib.lib().ts_attn_decode_noalloc(ctypes.byref(params), stream)
+    torch.cuda.synchronize()
+    del keep
+    return status, out, lse
+
+
+def test_noalloc_decode_matches_workspace_decode_twice():
+    problems = [
+        _problem(1, 8, 32, 8, 6000, [6000, 1, 4097, 2500, 33, 5999, 1024, 3000]),
+        _problem(2, 4, 16, 16, 3000, [7, 3000, 1500, 2049]),
+    ]
+    for q, k, v, kv_lens in problems:
+        need = engine.decode_workspace_bytes(q, k, v, is_causal=True, kv_lens=kv_lens)
+        assert 0 < need <= _lib.NOALLOC_SCRATCH_BYTES  # several splits, fits the scratch
+        ref, ref_lse = engine.decode(q, k, v, is_causal=True, kv_lens=kv_lens, need_lse=True)
+        status, out, lse = _noalloc(q, k, v, kv_lens)
+        assert status == _lib.OK, _lib.strerror(status)
+        engine.check_device_status()
+        err = (out.float() - ref.float()).abs().max().item()
+        scale = max(1.0, ref.float().abs().max().item())
+        assert err <= HALF_MAXABS * scale, f"max-abs {err:.3e}"
+        np.testing.assert_allclose(lse.cpu().numpy(), ref_lse.cpu().numpy(), rtol=2e-3, atol=2e-3)
+
+
+def test_noalloc_rejects_problems_larger_than_the_scratch():
+    q, k, v, kv_lens = _problem(3, 16, 64, 8, 16384, [16384] * 16)
+    need = engine.decode_workspace_bytes(q, k, v, is_causal=True, kv_lens=kv_lens)
+    assert need > _lib.NOALLOC_SCRATCH_BYTES
+    status, _, _ = _noalloc(q, k, v, kv_lens)
+    assert status == _lib.ERR_WORKSPACE
+    with pytest.raises(_lib.EngineError, match="8 MiB"):
+        engine.decode_noalloc(q, k, v, is_causal=True, kv_lens=kv_lens)
