@@ -6,6 +6,7 @@
 #include "decode.cuh"
 #include "kv_cache.cuh"
 #include "simt.cuh"
+#include "tc_bwd.cuh"
 #include "tc_fwd.cuh"
 
 namespace {
@@ -101,7 +102,15 @@ int ts_attn_decode(const ts_attn_params* p, void* workspace, size_t workspace_by
 
 size_t ts_attn_bwd_workspace_size(const ts_attn_bwd_params* bp) {
   if (!bp || check_params(&bp->fwd) != TS_OK) return 0;
+  if (tsa::tc_bwd_supported(*bp)) return tsa::tc_bwd_workspace(*bp);
   return tsa::simt_backward_workspace(*bp);
+}
+
+int ts_attn_bwd_path(const ts_attn_bwd_params* bp) {
+  if (!bp) return TS_ERR_INVALID_ARGUMENT;
+  const int st = check_params(&bp->fwd);
+  if (st != TS_OK) return st;
+  return tsa::tc_bwd_supported(*bp) ? TS_PATH_TCGEN05 : TS_PATH_SIMT;
 }
 
 int ts_attn_bwd(const ts_attn_bwd_params* bp, void* workspace, size_t workspace_bytes, void* stream) {
@@ -110,6 +119,10 @@ int ts_attn_bwd(const ts_attn_bwd_params* bp, void* workspace, size_t workspace_
   if (st != TS_OK) return st;
   if (!bp->fwd.lse || !bp->dout.data || !bp->dq.data || !bp->dk.data || !bp->dv.data)
     return TS_ERR_INVALID_ARGUMENT;
+  if (tsa::tc_bwd_supported(*bp)) {
+    if (!workspace || workspace_bytes < tsa::tc_bwd_workspace(*bp)) return TS_ERR_WORKSPACE;
+    return from_cuda(tsa::tc_backward(*bp, workspace, workspace_bytes, fault_ptr(), as_stream(stream)));
+  }
   const size_t need = tsa::simt_backward_workspace(*bp);
   if (!workspace || workspace_bytes < need) return TS_ERR_WORKSPACE;
   return from_cuda(tsa::simt_backward(*bp, workspace, as_stream(stream)));

@@ -1,0 +1,485 @@
+// Attention backward on the tcgen05 tensor cores for bf16 / f16 inputs with
+// D = Dv in {64, 128}.
+//
+// Replaces the blockwise VJP of tensorsmith's nn/attention.py:220-247: per
+// (query block, key block) p = exp(S - LSE), dS = p * (dO.V^T - rowsum(dO*O))
+// * scale, dQ += dS K, dK += dS^T Q, dV += p^T dO, with dK/dV summed over the
+// query heads of a KV group (:245-247).
+//
+// One CTA = 128 keys of one (batch, KV head); it loops over 64-row query tiles
+// of every query head of the group (causal: only tiles that see the keys).
+// Per query tile five MMAs run with TMEM accumulators (lane = key for the
+// first four, lane = channel for the last):
+//   S^T  = K  Q^T     [128 x 64]   A = K   (K-major)  B = Q   (K-major)
+//   dP^T = V  dO^T    [128 x 64]   A = V   (K-major)  B = dO  (K-major)
+//   dV  += P^T dO     [128 x Dv]   A = P^T (K-major)  B = dO  (MN-major)
+//   dK  += dS^T Q     [128 x D]    A = dS^T(K-major)  B = Q   (MN-major)
+//   dQ^T = K^T dS^T   [D x 64]     A = K   (MN-major) B = dS^T(MN-major)
+// P^T and dS^T are written by the "softmax" warpgroup (thread = key row) into
+// 128-byte-swizzled shared tiles that serve both as K-major A and MN-major B
+// operands.  dQ^T is read by the epilogue warpgroup (thread = channel) and
+// added into an fp32 dQ accumulator with coalesced atomics; a final kernel
+// converts it.  dK/dV stay in TMEM for the whole CTA (no atomics, GQA summed).
+//
+// Warps: 0 TMA producer, 1 MMA issuer, 2 TMEM allocator, 4-7 softmax
+// (P^T, dS^T, then the dK/dV epilogue), 8-11 dQ epilogue.  No TMA load uses
+// cluster multicast.
+#include <type_traits>
+
+#include "ptx.cuh"
+#include "simt.cuh"
+#include "tc_bwd.cuh"
+#include "tc_util.cuh"
+
+namespace tsa {
+
+namespace {
+
+constexpr int kBN = 128;  // keys per CTA
+constexpr int kBM = 64;   // query rows per iteration
+constexpr int kKSlab = 128 * 128;  // 128 rows x 128 B
+constexpr int kQSlab = 64 * 128;   // 64 rows x 128 B
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int D> struct BwdCfg {
+  static constexpr int kSlabs = D / 64;
+  static constexpr int kOffK = 0;
+  static constexpr int kOffV = kOffK + kSlabs * kKSlab;
+  static constexpr int kOffQ = kOffV + kSlabs * kKSlab;       // 2 stages
+  static constexpr int kOffDO = kOffQ + 2 * kSlabs * kQSlab;   // 2 stages
+  static constexpr int kOffP = kOffDO + 2 * kSlabs * kQSlab;
+  static constexpr int kOffDS = kOffP + kKSlab;
+  static constexpr int kOffStat = kOffDS + kKSlab;             // [2][2][64] floats
+  static constexpr int kOffBar = kOffStat + 2 * 2 * kBM * 4;
+  static constexpr int kUsed = kOffBar + 256 + 1024;
+  // One CTA per SM: the kernel owns all 512 TMEM columns.
+  static constexpr int kSmem = kUsed > 120 * 1024 ? kUsed : 120 * 1024;
+  static constexpr uint32_t kColDK = 0, kColDV = 128, kColS = 256, kColDP = 320, kColDQ = 384;
+};
+
+struct BwdBars {
+  uint64_t kv_full;
+  uint64_t qdo_full[2], qdo_empty[2];
+  uint64_t s_full, s_free, p_full, b_done, dq_free, drain;
+  uint32_t tmem_base;
+};
+
+struct TcBwdArgs {
+  ts_attn_params p;  // forward problem (q, k, v, o, lse)
+  ts_view4 dk, dv;
+  float* delta;      // [B, Hq, Tq]
+  float* dq_acc;     // [B, Hq, Tq, D]
+  int n_k_tiles;
+  uint32_t* fault;
+};
+
+}  // namespace
+
+template <int D, bool kBF16>
+__global__ void __launch_bounds__(384, 1)
+    tc_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                  TcBwdArgs args) {
+  using C = BwdCfg<D>;
+  using T = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
+  const ts_attn_params& p = args.p;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  BwdBars* bars = reinterpret_cast<BwdBars*>(smem + C::kOffBar);
+  unsigned char* sK = smem + C::kOffK;
+  unsigned char* sV = smem + C::kOffV;
+  unsigned char* sQ = smem + C::kOffQ;
+  unsigned char* sDO = smem + C::kOffDO;
+  unsigned char* sP = smem + C::kOffP;
+  unsigned char* sDS = smem + C::kOffDS;
+  float* sStat = reinterpret_cast<float*>(smem + C::kOffStat);  // [buf][lse2 | delta][64]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int rep = p.q_heads / p.kv_heads;
+  const int k0 = kt * kBN;
+
+  int kv_end = p.kv_len;
+  int64_t offset = p.causal_offset;
+  if (p.kv_lens) {
+    kv_end = min(kv_end, max(0, p.kv_lens[b]));
+    offset = (int64_t)kv_end - p.q_len;
+  }
+  const int n_qt_all = ceil_div(p.q_len, kBM);
+  int qt_start = 0;
+  if (p.is_causal) qt_start = (int)(i64max(0, (int64_t)k0 - offset) / kBM);
+  const int n_qt = k0 < kv_end ? max(0, n_qt_all - qt_start) : 0;
+  const int n_it = rep * n_qt;
+  const bool dead = fault_set(args.fault);
+
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(&bars->kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      ptx::mbar_init(&bars->qdo_full[s], 1);
+      ptx::mbar_init(&bars->qdo_empty[s], 1);
+    }
+    ptx::mbar_init(&bars->s_full, 1);
+    ptx::mbar_init(&bars->s_free, 4);
+    ptx::mbar_init(&bars->p_full, 4);
+    ptx::mbar_init(&bars->b_done, 1);
+    ptx::mbar_init(&bars->dq_free, 4);
+    ptx::mbar_init(&bars->drain, 1);
+    ptx::fence_mbar_init();
+  }
+  if (warp == 2) {
+    ptx::tmem_alloc(&bars->tmem_base, 512);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  auto it_head = [&](int it) { return hk * rep + it / n_qt; };
+  auto it_q0 = [&](int it) { return (qt_start + it % n_qt) * kBM; };
+
+  if (warp == 0) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0 && n_it > 0 && !dead) {
+      ptx::prefetch_tensormap(&tm_q);
+      ptx::prefetch_tensormap(&tm_k);
+      ptx::prefetch_tensormap(&tm_v);
+      ptx::prefetch_tensormap(&tm_do);
+      ptx::mbar_expect_tx(&bars->kv_full, 2 * C::kSlabs * kKSlab);
+      for (int sl = 0; sl < C::kSlabs; ++sl) {
+        ptx::tma_load_4d(sK + sl * kKSlab, &tm_k, 64 * sl, k0, hk, b, &bars->kv_full);
+        ptx::tma_load_4d(sV + sl * kKSlab, &tm_v, 64 * sl, k0, hk, b, &bars->kv_full);
+      }
+      int issued = 0;
+      for (int it = 0; it < n_it; ++it) {
+        const int s = it & 1;
+        if (it >= 2 && !wait_bar(&bars->qdo_empty[s], ((it >> 1) - 1) & 1, args.fault, FAULT_FWD_EMPTY)) break;
+        const int h = it_head(it), q0 = it_q0(it);
+        ptx::mbar_expect_tx(&bars->qdo_full[s], 2 * C::kSlabs * kQSlab);
+        for (int sl = 0; sl < C::kSlabs; ++sl) {
+          ptx::tma_load_4d(sQ + (s * C::kSlabs + sl) * kQSlab, &tm_q, 64 * sl, q0, h, b, &bars->qdo_full[s]);
+          ptx::tma_load_4d(sDO + (s * C::kSlabs + sl) * kQSlab, &tm_do, 64 * sl, q0, h, b, &bars->qdo_full[s]);
+        }
+        issued = it + 1;
+      }
+      (void)wait_bar(&bars->kv_full, 0, nullptr, FAULT_FWD_DRAIN);
+      for (int it = max(0, issued - 2); it < issued; ++it)
+        (void)wait_bar(&bars->qdo_full[it & 1], (it >> 1) & 1, nullptr, FAULT_FWD_DRAIN);
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ----------------------------
+    if (lane == 0 && n_it > 0 && !dead) {
+      constexpr uint32_t id_s = ptx::idesc_f16(kBF16, 128, kBM, false, false);
+      constexpr uint32_t id_dkv = ptx::idesc_f16(kBF16, 128, D, false, true);
+      constexpr uint32_t id_dq = ptx::idesc_f16(kBF16, 128, kBM, true, true);
+      const uint32_t aK = ptx::smem_u32(sK), aV = ptx::smem_u32(sV), aQ = ptx::smem_u32(sQ),
+                     aDO = ptx::smem_u32(sDO), aP = ptx::smem_u32(sP), aDS = ptx::smem_u32(sDS);
+      bool ok = wait_bar(&bars->kv_full, 0, args.fault, FAULT_FWD_KV);
+      auto issue_a = [&](int it) -> bool {
+        const int s = it & 1;
+        if (!wait_bar(&bars->qdo_full[s], (it >> 1) & 1, args.fault, FAULT_FWD_KV)) return false;
+        ptx::tc_fence_after();
+        const uint32_t q = aQ + s * C::kSlabs * kQSlab, dO = aDO + s * C::kSlabs * kQSlab;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t ko = (kk >> 2) * kKSlab + (kk & 3) * 32, qo = (kk >> 2) * kQSlab + (kk & 3) * 32;
+          ptx::mma_f16_ss(tmem + C::kColS, ptx::sw128_desc(aK + ko, 16, 1024), ptx::sw128_desc(q + qo, 16, 1024),
+                          id_s, kk > 0 ? 1u : 0u);
+          ptx::mma_f16_ss(tmem + C::kColDP, ptx::sw128_desc(aV + ko, 16, 1024),
+                          ptx::sw128_desc(dO + qo, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+        }
+        ptx::mma_commit(&bars->s_full);
+        return true;
+      };
+      if (ok) ok = issue_a(0);
+      for (int it = 0; it < n_it && ok; ++it) {
+        if (it + 1 < n_it) {
+          if (!wait_bar(&bars->s_free, it & 1, args.fault, FAULT_FWD_S) || !issue_a(it + 1)) {
+            ok = false;
+            break;
+          }
+        }
+        if (!wait_bar(&bars->p_full, it & 1, args.fault, FAULT_FWD_P) ||
+            (it >= 1 && !wait_bar(&bars->dq_free, (it - 1) & 1, args.fault, FAULT_FWD_O))) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const int s = it & 1;
+        const uint32_t q = aQ + s * C::kSlabs * kQSlab, dO = aDO + s * C::kSlabs * kQSlab;
+#pragma unroll
+        for (int kk = 0; kk < kBM / 16; ++kk) {
+          const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
+          ptx::mma_f16_ss(tmem + C::kColDV, ptx::sw128_desc(aP + kk * 32, 16, 1024),
+                          ptx::sw128_desc(dO + kk * 16 * 128, kQSlab, 1024), id_dkv, acc);
+          ptx::mma_f16_ss(tmem + C::kColDK, ptx::sw128_desc(aDS + kk * 32, 16, 1024),
+                          ptx::sw128_desc(q + kk * 16 * 128, kQSlab, 1024), id_dkv, acc);
+        }
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          ptx::mma_f16_ss(tmem + C::kColDQ, ptx::sw128_desc(aK + kk * 16 * 128, kKSlab, 1024),
+                          ptx::sw128_desc(aDS + kk * 16 * 128, kQSlab, 1024), id_dq, kk > 0 ? 1u : 0u);
+        ptx::mma_commit(&bars->b_done);
+        ptx::mma_commit(&bars->qdo_empty[s]);
+      }
+      ptx::mma_commit(&bars->drain);
+      (void)wait_bar(&bars->drain, 0, nullptr, FAULT_FWD_DRAIN);
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------- P^T / dS^T (thread = key row) ---------------------
+    const int row = (warp - 4) * 32 + lane;
+    const int key = k0 + row;
+    const uint32_t t_row = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const float sl2 = (float)p.scale * kLog2e, scale = (float)p.scale;
+    bool ok = !dead;
+    // Row statistics of iteration `it` (thread t < 64: LSE of row t; else delta of row t-64).
+    auto stat_value = [&](int it) -> float {
+      const int h = it_head(it), q0 = it_q0(it);
+      const int t = row & 63, i = q0 + t;
+      if (row < 64) {
+        if (i >= p.q_len) return INFINITY;
+        const float l = reinterpret_cast<const float*>(p.lse)[(int64_t)b * p.lse_stride[0] +
+                                                              (int64_t)h * p.lse_stride[1] +
+                                                              (int64_t)i * p.lse_stride[2]];
+        return l == -INFINITY ? INFINITY : l * kLog2e;  // fully masked row -> p = 0
+      }
+      return i < p.q_len ? args.delta[((int64_t)b * p.q_heads + h) * p.q_len + i] : 0.f;
+    };
+    if (n_it > 0) sStat[row] = stat_value(0);
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    // Every softmax warp runs all n_it iterations and reaches every named
+    // barrier; after a failed wait it only skips the work (no early exit).
+    for (int it = 0; it < n_it; ++it) {
+      const int q0 = it_q0(it);
+      const float next = (it + 1 < n_it) ? stat_value(it + 1) : 0.f;
+      const float* lse2 = sStat + (it & 1) * 128;
+      const float* dlt = lse2 + 64;
+      // Warp-uniform outcomes: the tcgen05.ld below are warp-collective.
+      if (ok) ok = __all_sync(0xffffffffu, wait_bar(&bars->s_full, it & 1, args.fault, FAULT_FWD_S));
+      if (ok) {
+        ptx::tc_fence_after();
+        const bool key_ok = key < kv_end;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t rs[32], rd[32];
+          ptx::tmem_ld32(t_row + C::kColS + 32 * half, rs);
+          ptx::tmem_ld32(t_row + C::kColDP + 32 * half, rd);
+          ptx::tmem_wait_ld();
+          if (half == 1) {
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&bars->s_free);
+          }
+          uint32_t pk[16], dk[16];
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            float pv[2], dsv[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int col = 32 * half + c + e;
+              const int64_t i = q0 + col;
+              const bool vis = key_ok && (!p.is_causal || i + offset >= key);
+              const float pr = vis ? ptx::ex2(__uint_as_float(rs[c + e]) * sl2 - lse2[col]) : 0.f;
+              pv[e] = pr;
+              dsv[e] = pr * (__uint_as_float(rd[c + e]) - dlt[col]) * scale;
+            }
+            pk[c / 2] = kBF16 ? ptx::pack_bf16(pv[0], pv[1]) : ptx::pack_f16(pv[0], pv[1]);
+            dk[c / 2] = kBF16 ? ptx::pack_bf16(dsv[0], dsv[1]) : ptx::pack_f16(dsv[0], dsv[1]);
+          }
+          // P^T / dS^T buffers are free once the previous iteration's dV/dK/dQ MMAs completed.
+          if (half == 0 && it >= 1)
+            ok = __all_sync(0xffffffffu, wait_bar(&bars->b_done, (it - 1) & 1, args.fault, FAULT_FWD_O));
+          if (ok) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const int chunk = half * 4 + c;
+              const int off = row * 128 + ((chunk ^ (row & 7)) << 4);
+              *reinterpret_cast<uint4*>(sP + off) =
+                  make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+              *reinterpret_cast<uint4*>(sDS + off) =
+                  make_uint4(dk[4 * c], dk[4 * c + 1], dk[4 * c + 2], dk[4 * c + 3]);
+            }
+          }
+        }
+        if (ok) {
+          ptx::fence_proxy_async_smem();
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&bars->p_full);
+        }
+      }
+      sStat[((it + 1) & 1) * 128 + row] = next;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+    }
+    // dK / dV epilogue: TMEM rows -> global.
+    if (ok && n_it > 0)
+      ok = __all_sync(0xffffffffu, wait_bar(&bars->b_done, (n_it - 1) & 1, args.fault, FAULT_FWD_O));
+    ptx::tc_fence_after();
+    // tcgen05.ld is warp-collective (.sync.aligned): every lane loads, and only
+    // the global stores are predicated on the key being inside the tensor.
+    const bool store_row = key < p.kv_len;
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+      const ts_view4& dst = which == 0 ? args.dk : args.dv;
+      T* out = reinterpret_cast<T*>(dst.data) + (int64_t)b * dst.stride[0] + (int64_t)hk * dst.stride[1] +
+               (int64_t)key * dst.stride[2];
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        if (ok && n_it > 0) {
+          ptx::tmem_ld32(t_row + (which == 0 ? C::kColDK : C::kColDV) + 32 * c, r);
+          ptx::tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = 0u;
+        }
+        if (store_row) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            const float* f = reinterpret_cast<const float*>(r + e);
+            uint4 v;
+            if (kBF16)
+              v = make_uint4(ptx::pack_bf16(f[0], f[1]), ptx::pack_bf16(f[2], f[3]), ptx::pack_bf16(f[4], f[5]),
+                             ptx::pack_bf16(f[6], f[7]));
+            else
+              v = make_uint4(ptx::pack_f16(f[0], f[1]), ptx::pack_f16(f[2], f[3]), ptx::pack_f16(f[4], f[5]),
+                             ptx::pack_f16(f[6], f[7]));
+            *reinterpret_cast<uint4*>(out + 32 * c + e) = v;
+          }
+        }
+      }
+    }
+  } else if (warp >= 8) {
+    // ----------------------- dQ epilogue (thread = channel) ----------------
+    const int d = (warp - 8) * 32 + lane;
+    const uint32_t t_row = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    bool ok = !dead;
+    for (int it = 0; it < n_it && ok; ++it) {
+      if (!__all_sync(0xffffffffu, wait_bar(&bars->b_done, it & 1, args.fault, FAULT_FWD_O))) {
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      uint32_t r0[32], r1[32];
+      ptx::tmem_ld32(t_row + C::kColDQ, r0);
+      ptx::tmem_ld32(t_row + C::kColDQ + 32, r1);
+      ptx::tmem_wait_ld();
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&bars->dq_free);
+      if (d < D) {
+        const int h = it_head(it), q0 = it_q0(it);
+        float* acc = args.dq_acc + (((int64_t)b * p.q_heads + h) * p.q_len + q0) * D + d;
+        const int rows = min(kBM, p.q_len - q0);
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          if (c < rows) atomicAdd(acc + (int64_t)c * D, __uint_as_float(r0[c]));
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          if (32 + c < rows) atomicAdd(acc + (int64_t)(32 + c) * D, __uint_as_float(r1[c]));
+      }
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, 512);
+  }
+}
+
+// dq[b,h,i,:] = dq_acc (fp32) converted to the input dtype.
+template <typename T>
+__global__ void dq_convert_kernel(const float* __restrict__ acc, ts_view4 dq, int heads, int len, int dim,
+                                  int64_t total) {
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int d = (int)(idx % dim);
+    const int64_t r = idx / dim;
+    const int i = (int)(r % len), h = (int)((r / len) % heads), b = (int)(r / ((int64_t)len * heads));
+    reinterpret_cast<T*>(dq.data)[(int64_t)b * dq.stride[0] + (int64_t)h * dq.stride[1] +
+                                  (int64_t)i * dq.stride[2] + (int64_t)d * dq.stride[3]] =
+        Elem<T>::from_acc(acc[idx]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+static bool out_rows_ok(const ts_view4& v) {
+  return v.stride[3] == 1 && reinterpret_cast<uintptr_t>(v.data) % 16 == 0 && (v.stride[2] * 2) % 16 == 0 &&
+         (v.stride[1] * 2) % 16 == 0 && (v.stride[0] * 2) % 16 == 0;
+}
+
+bool tc_bwd_supported(const ts_attn_bwd_params& bp) {
+  const ts_attn_params& p = bp.fwd;
+  if (p.dtype != TS_BF16 && p.dtype != TS_F16) return false;
+  if (p.head_dim != p.value_dim || (p.head_dim != 64 && p.head_dim != 128)) return false;
+  if (p.mask_kind != TS_MASK_NONE || !p.lse) return false;
+  if (!view_tma_ok(p.q) || !view_tma_ok(p.k) || !view_tma_ok(p.v) || !view_tma_ok(bp.dout)) return false;
+  if (!out_rows_ok(bp.dk) || !out_rows_ok(bp.dv)) return false;
+  return encode_fn() != nullptr;
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+size_t tc_bwd_workspace(const ts_attn_bwd_params& bp) {
+  const ts_attn_params& p = bp.fwd;
+  const size_t rows = (size_t)p.batch * p.q_heads * p.q_len;
+  return align256(rows * sizeof(float)) + align256(rows * p.head_dim * sizeof(float));
+}
+
+template <int D, bool BF16>
+static cudaError_t launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                              const CUtensorMap& mdo, const TcBwdArgs& a, cudaStream_t st) {
+  auto kern = tc_bwd_kernel<D, BF16>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdCfg<D>::kSmem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(a.n_k_tiles, a.p.kv_heads, a.p.batch);
+  kern<<<grid, 384, BwdCfg<D>::kSmem, st>>>(mq, mk, mv, mdo, a);
+  return cudaGetLastError();
+}
+
+cudaError_t tc_backward(const ts_attn_bwd_params& bp, void* ws, size_t ws_bytes, uint32_t* fault,
+                        cudaStream_t st) {
+  const ts_attn_params& p = bp.fwd;
+  if (ws_bytes < tc_bwd_workspace(bp)) return cudaErrorInvalidValue;
+  const size_t rows = (size_t)p.batch * p.q_heads * p.q_len;
+  float* delta = reinterpret_cast<float*>(ws);
+  float* dq_acc = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(ws) + align256(rows * sizeof(float)));
+  CUtensorMap mq, mk, mv, mdo;
+  if (!make_map(&mq, p.q, p.dtype, p.batch, p.q_heads, p.q_len, p.head_dim, kBM) ||
+      !make_map(&mk, p.k, p.dtype, p.batch, p.kv_heads, p.kv_len, p.head_dim, kBN) ||
+      !make_map(&mv, p.v, p.dtype, p.batch, p.kv_heads, p.kv_len, p.value_dim, kBN) ||
+      !make_map(&mdo, bp.dout, p.dtype, p.batch, p.q_heads, p.q_len, p.value_dim, kBM))
+    return cudaErrorInvalidValue;
+  cudaError_t e = simt_delta_f32(bp, delta, st);
+  if (e != cudaSuccess) return e;
+  e = cudaMemsetAsync(dq_acc, 0, rows * p.head_dim * sizeof(float), st);
+  if (e != cudaSuccess) return e;
+  TcBwdArgs a;
+  a.p = p;
+  a.dk = bp.dk;
+  a.dv = bp.dv;
+  a.delta = delta;
+  a.dq_acc = dq_acc;
+  a.n_k_tiles = ceil_div(p.kv_len, kBN);
+  a.fault = fault;
+  const bool bf = p.dtype == TS_BF16;
+  if (p.head_dim == 64)
+    e = bf ? launch_bwd<64, true>(mq, mk, mv, mdo, a, st) : launch_bwd<64, false>(mq, mk, mv, mdo, a, st);
+  else
+    e = bf ? launch_bwd<128, true>(mq, mk, mv, mdo, a, st) : launch_bwd<128, false>(mq, mk, mv, mdo, a, st);
+  if (e != cudaSuccess) return e;
+  const int64_t total = (int64_t)rows * p.head_dim;
+  const int blocks = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
+  if (bf)
+    dq_convert_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(dq_acc, bp.dq, p.q_heads, p.q_len, p.head_dim, total);
+  else
+    dq_convert_kernel<__half><<<blocks, 256, 0, st>>>(dq_acc, bp.dq, p.q_heads, p.q_len, p.head_dim, total);
+  return cudaGetLastError();
+}
+
+}  // namespace tsa

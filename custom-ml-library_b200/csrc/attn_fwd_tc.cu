@@ -26,6 +26,7 @@
 
 #include "ptx.cuh"
 #include "tc_fwd.cuh"
+#include "tc_util.cuh"
 
 namespace tsa {
 
@@ -70,27 +71,6 @@ struct TcFwdArgs {
   int n_q_tiles;
   uint32_t* fault;
 };
-
-__device__ __forceinline__ bool fault_set(const uint32_t* fault) {
-  return fault && *reinterpret_cast<const volatile uint32_t*>(fault) != 0u;
-}
-
-// Bounded wait that also gives up as soon as any CTA recorded a fault.
-__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, uint32_t* fault,
-                                         uint32_t site) {
-  if (ptx::mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (ptx::mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0u) {
-      if (fault_set(fault)) return false;
-      if (global_ns() - t0 > kWaitLimitNs) {
-        record_fault(fault, site);
-        return false;
-      }
-    }
-  }
-}
 
 }  // namespace
 
@@ -245,7 +225,8 @@ __global__ void __launch_bounds__(256, 1)
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = !dead;
     for (int j = 0; j < n_tiles && ok; ++j) {
-      if (!wait_bar(&bars->s_full[j & 1], (j >> 1) & 1, args.fault, FAULT_FWD_S)) {
+      // Warp-uniform outcome: the tcgen05.ld/st below are warp-collective.
+      if (!__all_sync(0xffffffffu, wait_bar(&bars->s_full[j & 1], (j >> 1) & 1, args.fault, FAULT_FWD_S))) {
         ok = false;
         break;
       }
@@ -295,12 +276,15 @@ __global__ void __launch_bounds__(256, 1)
       }
       l_run += sum;
       // P buffer and O are free once P(j-1).V(j-1) has completed.
-      if (j >= 1 && !wait_bar(&bars->o_done, (j - 1) & 1, args.fault, FAULT_FWD_O)) {
+      if (j >= 1 && !__all_sync(0xffffffffu, wait_bar(&bars->o_done, (j - 1) & 1, args.fault, FAULT_FWD_O))) {
         ok = false;
         break;
       }
       ptx::tc_fence_after();
-      if (rescale && j >= 1) {
+      // The rescale decision is per row; the TMEM round trip is warp-collective,
+      // so the whole warp takes it when any row needs it (factor 1 elsewhere).
+      if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
+        if (!rescale) factor = 1.f;
         uint32_t r[32];
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
@@ -328,7 +312,8 @@ __global__ void __launch_bounds__(256, 1)
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&bars->p_full);
     }
-    if (ok && n_tiles > 0) ok = wait_bar(&bars->o_done, (n_tiles - 1) & 1, args.fault, FAULT_FWD_O);
+    if (ok && n_tiles > 0)
+      ok = __all_sync(0xffffffffu, wait_bar(&bars->o_done, (n_tiles - 1) & 1, args.fault, FAULT_FWD_O));
     ptx::tc_fence_after();
     // Epilogue: O / l -> global, LSE.
     const bool live_row = qi < p.q_len;
@@ -378,33 +363,6 @@ __global__ void __launch_bounds__(256, 1)
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
-                                  CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
-                                  CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  }
-  return fn;
-}
-
-static bool view_tma_ok(const ts_view4& v) {
-  if (v.stride[3] != 1) return false;
-  if (reinterpret_cast<uintptr_t>(v.data) % 16) return false;
-  for (int i = 0; i < 3; ++i)
-    if ((v.stride[i] * 2) % 16 || v.stride[i] <= 0) return false;
-  return true;
-}
-
 bool tc_fwd_supported(const ts_attn_params& p) {
   if (p.dtype != TS_BF16 && p.dtype != TS_F16) return false;
   if (p.head_dim != p.value_dim || (p.head_dim != 64 && p.head_dim != 128)) return false;
@@ -414,20 +372,6 @@ bool tc_fwd_supported(const ts_attn_params& p) {
       (p.o.stride[1] * 2) % 16 || (p.o.stride[0] * 2) % 16)
     return false;
   return encode_fn() != nullptr;
-}
-
-static bool make_map(CUtensorMap* map, const ts_view4& v, int dtype, int batch, int heads, int len,
-                     int channels) {
-  const cuuint64_t dims[4] = {(cuuint64_t)channels, (cuuint64_t)len, (cuuint64_t)heads, (cuuint64_t)batch};
-  const cuuint64_t strides[3] = {(cuuint64_t)v.stride[2] * 2, (cuuint64_t)v.stride[1] * 2,
-                                 (cuuint64_t)v.stride[0] * 2};
-  const cuuint32_t box[4] = {64, 128, 1, 1};
-  const cuuint32_t estr[4] = {1, 1, 1, 1};
-  const CUtensorMapDataType dt =
-      dtype == TS_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  return encode_fn()(map, dt, 4, v.data, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <int D, bool BF16>
@@ -443,9 +387,9 @@ static cudaError_t launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, const
 
 cudaError_t tc_forward(const ts_attn_params& p, uint32_t* fault, cudaStream_t st) {
   CUtensorMap mq, mk, mv;
-  if (!make_map(&mq, p.q, p.dtype, p.batch, p.q_heads, p.q_len, p.head_dim) ||
-      !make_map(&mk, p.k, p.dtype, p.batch, p.kv_heads, p.kv_len, p.head_dim) ||
-      !make_map(&mv, p.v, p.dtype, p.batch, p.kv_heads, p.kv_len, p.value_dim))
+  if (!make_map(&mq, p.q, p.dtype, p.batch, p.q_heads, p.q_len, p.head_dim, 128) ||
+      !make_map(&mk, p.k, p.dtype, p.batch, p.kv_heads, p.kv_len, p.head_dim, 128) ||
+      !make_map(&mv, p.v, p.dtype, p.batch, p.kv_heads, p.kv_len, p.value_dim, 128))
     return cudaErrorInvalidValue;
   TcFwdArgs a;
   a.p = p;

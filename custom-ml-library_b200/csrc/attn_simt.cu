@@ -451,6 +451,18 @@ static cudaError_t simt_bwd_t(const ts_attn_bwd_params& bp, void* ws, cudaStream
   }
 }
 
+cudaError_t simt_delta_f32(const ts_attn_bwd_params& bp, float* delta, cudaStream_t st) {
+  const int rows = bp.fwd.batch * bp.fwd.q_heads * bp.fwd.q_len;
+  const dim3 grid(ceil_div(rows * 32, 256));
+  switch (bp.fwd.dtype) {
+    case TS_F32: simt_bwd_delta_kernel<float><<<grid, 256, 0, st>>>(bp, delta); break;
+    case TS_F16: simt_bwd_delta_kernel<__half><<<grid, 256, 0, st>>>(bp, delta); break;
+    case TS_BF16: simt_bwd_delta_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(bp, delta); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
 cudaError_t simt_forward(const ts_attn_params& p, cudaStream_t st) {
   switch (p.dtype) {
     case TS_F32: return simt_fwd_t<float>(p, st);

@@ -7,6 +7,8 @@ namespace tsa {
 cudaError_t simt_forward(const ts_attn_params& p, cudaStream_t stream);
 // Bytes of workspace simt_backward needs (row deltas in the accumulation type).
 size_t simt_backward_workspace(const ts_attn_bwd_params& bp);
+// delta[b,h,i] = sum_c dO * O in fp32 (half / fp32 inputs), the backward preprocess.
+cudaError_t simt_delta_f32(const ts_attn_bwd_params& bp, float* delta, cudaStream_t stream);
 // dQ, dK, dV from the saved LSE.
 cudaError_t simt_backward(const ts_attn_bwd_params& bp, void* workspace, cudaStream_t stream);
 }  // namespace tsa

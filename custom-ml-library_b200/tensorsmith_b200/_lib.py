@@ -96,6 +96,7 @@ SIGNATURES = {
     "ts_attn_fwd_path": (ctypes.c_int, [ctypes.POINTER(AttnParams), ctypes.c_int]),
     "ts_attn_fwd": (ctypes.c_int, [ctypes.POINTER(AttnParams), ctypes.c_void_p]),
     "ts_attn_bwd_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(AttnBwdParams)]),
+    "ts_attn_bwd_path": (ctypes.c_int, [ctypes.POINTER(AttnBwdParams)]),
     "ts_attn_bwd": (
         ctypes.c_int,
         [ctypes.POINTER(AttnBwdParams), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p],

@@ -201,6 +201,24 @@ def decode_noalloc(q, k, v, *, is_causal=True, scale=None, causal_offset=0, kv_l
     return out, (lse if need_lse else None)
 
 
+def _bwd_params(q, k, v, out, lse, dout, dq, dk, dv, **kw):
+    fp, keep = make_params(q, k, v, out, lse, **kw)
+    bp = _lib.AttnBwdParams()
+    bp.fwd = fp
+    bp.dout, bp.dq, bp.dk, bp.dv = view4(dout), view4(dq), view4(dk), view4(dv)
+    return bp, keep
+
+
+def bwd_path(q, k, v, out, lse, dout, **kw) -> str:
+    """Name of the kernel family ts_attn_bwd selects for this problem."""
+    bp, keep = _bwd_params(q, k, v, out, lse, dout, torch.empty_like(q), torch.empty_like(k),
+                           torch.empty_like(v), **kw)
+    code = _lib.lib().ts_attn_bwd_path(ctypes.byref(bp))
+    if code < 0:
+        _lib.check(code, "ts_attn_bwd_path")
+    return _lib.PATH_NAMES[code]
+
+
 def backward(q, k, v, out, lse, dout, *, is_causal=False, scale=None, causal_offset=0, kv_lens=None,
              mask=None, dq=None, dk=None, dv=None):
     """dQ, dK, dV of attention from the forward output and its LSE."""
@@ -211,11 +229,8 @@ def backward(q, k, v, out, lse, dout, *, is_causal=False, scale=None, causal_off
     dv = torch.empty_like(v) if dv is None else dv
     if dout.dtype != q.dtype:
         dout = dout.to(q.dtype)
-    fp, keep = make_params(q, k, v, out, lse, is_causal=is_causal, scale=scale,
+    bp, keep = _bwd_params(q, k, v, out, lse, dout, dq, dk, dv, is_causal=is_causal, scale=scale,
                            causal_offset=causal_offset, kv_lens=kv_lens, mask=mask)
-    bp = _lib.AttnBwdParams()
-    bp.fwd = fp
-    bp.dout, bp.dq, bp.dk, bp.dv = view4(dout), view4(dq), view4(dk), view4(dv)
     handle = _lib.lib()
     need = int(handle.ts_attn_bwd_workspace_size(ctypes.byref(bp)))
     ws = torch.empty(max(need, 16), dtype=torch.uint8, device=q.device)

@@ -129,8 +129,13 @@ TS_ATTN_API int ts_attn_fwd_path(const ts_attn_params* params, int decode);
  * :146-174 is where tensorsmith plugs a vendor kernel). */
 TS_ATTN_API int ts_attn_fwd(const ts_attn_params* params, void* stream);
 
-/* Workspace bytes ts_attn_bwd needs (fp32 row statistics). */
+/* Workspace bytes ts_attn_bwd needs (fp32 row statistics, plus an fp32 dQ
+ * accumulator on the tensor-core path). */
 TS_ATTN_API size_t ts_attn_bwd_workspace_size(const ts_attn_bwd_params* params);
+
+/* Kernel family ts_attn_bwd would run (TS_PATH_TCGEN05 or TS_PATH_SIMT), or a
+ * negative ts_status when the parameters are invalid. */
+TS_ATTN_API int ts_attn_bwd_path(const ts_attn_bwd_params* params);
 
 /* Backward: dQ, dK, dV from recomputed probabilities (LSE of the forward).
  * Replaces the dense / blockwise VJP and the GQA reduction of
