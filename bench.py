@@ -43,6 +43,10 @@ WORKLOADS = {
     "c5": dict(batch=32, heads=32, head_dim=128, prefill=32768, decode_steps=128),
     # reduced shape of the same kernels, for profiler captures only
     "small": dict(batch=4, heads=32, head_dim=128, prefill=4096, decode_steps=4),
+    # causal prefill bf16 forward + backward
+    "c3": dict(batch=8, heads=16, head_dim=128, prefill=4096),
+    # fp16 KV-cache decode, ragged lengths U[1024, 8192], 256 steps with append
+    "c4": dict(batch=64, heads=32, head_dim=128, min_len=1024, max_len=8192, decode_steps=256),
 }
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -462,6 +466,176 @@ def run_e2e(args, cfg, plan, rank, world, local_rank, q, kc, vc, qd, kd, vd, ws,
             "path": "tensorsmith_b200.engine (C ABI) with pinned host inputs/outputs"}
 
 
+def _timed(args, step, n_events):
+    """Warm up, then time ``args.steps`` calls of ``step(events)`` with CUDA events."""
+    import torch
+
+    from tensorsmith_b200 import engine
+
+    for _ in range(args.warmup):
+        step([torch.cuda.Event(enable_timing=True) for _ in range(n_events)])
+    torch.cuda.synchronize()
+    engine.check_device_status()
+    sampler = ClockSampler(torch.cuda.current_device())
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_events)] for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for ev in evs:
+        step(ev)
+    t1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    engine.check_device_status()
+    return evs, t0.elapsed_time(t1) / args.steps, clocks
+
+
+def run_c3(args):
+    """Causal prefill bf16 B=8 H=16 T=4096 D=128: forward + backward."""
+    import numpy as np
+    import torch
+
+    from tensorsmith_b200 import engine
+
+    cfg = WORKLOADS["c3"]
+    B, H, T, D = cfg["batch"], cfg["heads"], cfg["prefill"], cfg["head_dim"]
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2)
+    q, k, v = ((torch.randn(B, H, T, D, generator=gen, device=dev) / D ** 0.5).to(torch.bfloat16) for _ in range(3))
+    do = torch.randn(B, H, T, D, generator=gen, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    lse = torch.empty(B, H, T, dtype=torch.float32, device=dev)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def step(ev):
+        ev[0].record()
+        engine.forward(q, k, v, is_causal=True, out=out, lse=lse)
+        ev[1].record()
+        engine.backward(q, k, v, out, lse, do, is_causal=True, dq=dq, dk=dk, dv=dv)
+        ev[2].record()
+
+    evs, step_ms, clocks = _timed(args, step, 3)
+    fwd = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    bwd = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    pairs_flops = causal_flops(B * H, T, T, 0, D) / 4.0  # D * P
+    peaks, src = load_peaks()
+    value = 14.0 * pairs_flops / ((fwd + bwd) / 1e3) / 1e12
+    bwd_tf = 10.0 * pairs_flops / (bwd / 1e3) / 1e12
+    fwd_tf = 4.0 * pairs_flops / (fwd / 1e3) / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"c3: causal attention bf16 B={B} H={H} T={T} D={D}, forward + backward, "
+                               "Q/K/V ~ N(0,1)/sqrt(128), dO ~ N(0,1)",
+                   "l2": "inputs larger than L2 (0.7 GB per step)"},
+        "forward": {"tflops": fwd_tf, "ms": fwd, "frac_of_measured_bf16": fwd_tf / peaks["bf16_tflops"]},
+        "backward": {"tflops": bwd_tf, "ms": bwd, "frac_of_measured_bf16": bwd_tf / peaks["bf16_tflops"],
+                     "launches": "delta preprocess + dQ zero + tc_bwd_kernel + dQ convert"},
+        "roofline": {"bound": "tensor", "kernel": "backward call (tc_bwd_kernel dominant)", "achieved": bwd_tf,
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": bwd_tf / peaks["bf16_tflops"],
+                     "peak_source": f"{src} bf16_tflops (burst; the call runs ~ms)", "traffic": None,
+                     "algorithmic": f"10*D*causal_pairs = {10 * pairs_flops:.4g} FLOP per backward call"},
+        "gpu_launches": 5 * args.steps,
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_c3_baseline(cfg, args.cpu_seconds)
+    return line
+
+
+def cpu_c3_baseline(cfg, budget_s):
+    """Oracle streaming forward + blockwise backward on one (b,h) slice, rows sub-sampled."""
+    import numpy as np
+
+    import oracle
+
+    T, D = cfg["prefill"], cfg["head_dim"]
+    rows = 512
+    rng = np.random.default_rng(3)
+    q = (rng.standard_normal((1, 1, rows, D)) / D ** 0.5).astype(np.float32)
+    k = (rng.standard_normal((1, 1, T, D)) / D ** 0.5).astype(np.float32)
+    v = (rng.standard_normal((1, 1, T, D)) / D ** 0.5).astype(np.float32)
+    g = rng.standard_normal((1, 1, rows, D)).astype(np.float32)
+    flops = 14.0 * causal_flops(1, rows, T, T - rows, D) / 4.0
+    times, start = [], time.perf_counter()
+    while not times or (time.perf_counter() - start < budget_s and len(times) < 20):
+        t0 = time.perf_counter()
+        o, l = oracle.attention_forward(q, k, v, is_causal=True, causal_offset=T - rows, algorithm="streaming",
+                                        block_size=1024)
+        oracle.attention_backward(q, k, v, o, l, g, is_causal=True, causal_offset=T - rows, block_size=1024)
+        times.append(time.perf_counter() - t0)
+    return {"value": flops / statistics.median(times) / 1e12, "unit": "TFLOP/s", "cores": cpu_cores(),
+            "kind": "port", "sample": f"oracle fwd+bwd (NumPy fp32, block 1024) of the last {rows} query rows of "
+                                      f"one (b,h) slice vs T={T} keys, median of {len(times)} reps"}
+
+
+def run_c4(args):
+    """fp16 KV-cache decode, B=64 H=32 D=128, ragged lengths, 256 steps with append."""
+    import numpy as np
+    import torch
+
+    from tensorsmith_b200 import engine
+
+    cfg = WORKLOADS["c4"]
+    B, H, D, S = cfg["batch"], cfg["heads"], cfg["head_dim"], cfg["decode_steps"]
+    cap = cfg["max_len"] + S
+    dev = torch.device("cuda", 0)
+    lens0 = np.random.default_rng(4).integers(cfg["min_len"], cfg["max_len"] + 1, B)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4)
+    kc = torch.randn(B, H, cap, D, generator=gen, device=dev).to(torch.float16)
+    vc = torch.randn(B, H, cap, D, generator=gen, device=dev).to(torch.float16)
+    qn, kn, vn = (torch.randn(S, B, H, 1, D, generator=gen, device=dev).to(torch.float16) for _ in range(3))
+    out = torch.empty(S, B, H, 1, D, dtype=torch.float16, device=dev)
+    start_lens = torch.tensor(lens0, dtype=torch.int32, device=dev)
+    lens = [torch.empty_like(start_lens), torch.empty_like(start_lens)]
+    ws = torch.empty(max(16, engine.decode_workspace_bytes(qn[0], kc, vc, is_causal=True, kv_lens=start_lens)),
+                     dtype=torch.uint8, device=dev)
+    splits = ws.numel() > 16
+
+    def step(ev):
+        lens[0].copy_(start_lens)
+        ev[0].record()
+        for s in range(S):
+            cur, nxt = lens[s & 1], lens[(s + 1) & 1]
+            engine.kv_append(kn[s], vn[s], kc, vc, positions=cur, positions_out=nxt)
+            engine.decode(qn[s], kc, vc, is_causal=True, kv_lens=nxt, out=out[s], workspace=ws)
+        ev[1].record()
+
+    evs, step_ms, clocks = _timed(args, step, 2)
+    dec = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    kv_bytes = float(sum(2 * H * D * 2 * (lens0 + s + 1).sum() for s in range(S)))
+    peaks, src = load_peaks()
+    gbs = kv_bytes / (dec / 1e3) / 1e9
+    tokens = B * S / (dec / 1e3)
+    line = {
+        "metric": METRIC, "value": tokens, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"c4: fp16 KV-cache decode B={B} H={H} D={D}, lengths U[{cfg['min_len']},"
+                               f"{cfg['max_len']}] per row, {S} decode steps each appending one token",
+                   "l2": "cache 8.9 GB, larger than L2"},
+        "decode": {"tokens_per_s": tokens, "hbm_gbs": gbs, "ms_per_token_step": dec / S,
+                   "frac_of_measured_hbm": gbs / peaks["hbm_gbs"], "frac_of_nominal_8000": gbs / 8000.0},
+        "roofline": {"bound": "hbm", "kernel": "decode step (kv_append + decode_split + combine)", "achieved": gbs,
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"],
+                     "peak_source": f"{src} hbm_gbs", "traffic": None,
+                     "algorithmic": "sum_b 2*H*L_b*D*2 bytes (K+V fp16 read) per step"},
+        "gpu_launches": S * (2 + (1 if splits else 0)) * args.steps,
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline:
+        cfg5 = dict(prefill=cfg["max_len"], head_dim=D)
+        per_pair, bpp = cpu_decode_sample(cfg5, 2)
+        mean_len = float(lens0.mean())
+        per_pair *= mean_len / cfg["max_len"]
+        line["cpu_baseline"] = {"value": B / (per_pair * B * H), "unit": "tokens/s", "cores": cpu_cores(),
+                                "kind": "port", "sample": "oracle dense decode of 2 (b,h) pairs vs an fp16 cache "
+                                f"of {cfg['max_len']} keys, scaled to the mean length {mean_len:.0f}"}
+    return line
+
+
 def main():
     args = parse_args()
     rank = int(os.environ.get("RANK", 0))
@@ -480,7 +654,12 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        result = run_engine(args, rank, world, local_rank)
+        if args.workload in ("c3", "c4"):
+            if world > 1:
+                raise SystemExit("the c3 / c4 parity configs run on one GPU; c5 is the multi-GPU workload")
+            result = (run_c3 if args.workload == "c3" else run_c4)(args)
+        else:
+            result = run_engine(args, rank, world, local_rank)
         if rank == 0 and result is not None:
             print(json.dumps(result), flush=True)
     finally:
