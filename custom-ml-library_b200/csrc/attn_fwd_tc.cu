@@ -231,31 +231,36 @@ __global__ void __launch_bounds__(256, 1)
         break;
       }
       ptx::tc_fence_after();
-      float x[kBN];
-      {
-        uint32_t r[32];
+      // All 128 raw scores of the row in registers (four loads, one wait).
+      uint32_t r[kBN];
 #pragma unroll
-        for (int c = 0; c < kBN / 32; ++c) {
-          ptx::tmem_ld32(t_row + C::kColS + (uint32_t)(j & 1) * kBN + 32 * c, r);
-          ptx::tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) x[32 * c + e] = __uint_as_float(r[e]) * qk_scale;
-        }
-      }
+      for (int c = 0; c < kBN / 32; ++c)
+        ptx::tmem_ld32(t_row + C::kColS + (uint32_t)(j & 1) * kBN + 32 * c,
+                       *reinterpret_cast<uint32_t(*)[32]>(r + 32 * c));
+      ptx::tmem_wait_ld();
       const int k0 = j * kBN;
       const bool need_mask = (k0 + kBN > kv_end) || (p.is_causal && (int64_t)k0 + kBN - 1 > (int64_t)q0 + offset);
-      if (need_mask) {
-        const int64_t lim = p.is_causal ? (int64_t)qi + offset : (int64_t)kv_end;
+      const int64_t lim = p.is_causal ? (int64_t)qi + offset : (int64_t)kv_end - 1;
+      // Row max of the (masked) raw scores, scaled once (scale > 0).  Tiles
+      // away from the diagonal and the sequence end take the unmasked branch
+      // (warp-uniform).
+      float mx = -INFINITY;
+      if (!need_mask) {
+        float m0 = -INFINITY, m1 = -INFINITY;  // two chains halve the dependent-max latency
+#pragma unroll
+        for (int c = 0; c < kBN; c += 4) {
+          m0 = ptx::max3(m0, __uint_as_float(r[c]), __uint_as_float(r[c + 1]));
+          m1 = ptx::max3(m1, __uint_as_float(r[c + 2]), __uint_as_float(r[c + 3]));
+        }
+        mx = fmaxf(m0, m1);
+      } else {
 #pragma unroll
         for (int c = 0; c < kBN; ++c) {
           const int key = k0 + c;
-          const bool vis = key < kv_end && (int64_t)key <= lim;
-          x[c] = vis ? x[c] : -INFINITY;
+          if (key < kv_end && (int64_t)key <= lim) mx = fmaxf(mx, __uint_as_float(r[c]));
         }
       }
-      float mx = x[0];
-#pragma unroll
-      for (int c = 1; c < kBN; ++c) mx = fmaxf(mx, x[c]);
+      mx = mx == -INFINITY ? mx : mx * qk_scale;
       const float m_new = fmaxf(m_run, mx);
       const bool rescale = m_new > m_run + kRescaleThreshold ||
                            (m_run == -INFINITY && m_new != -INFINITY);
@@ -266,15 +271,48 @@ __global__ void __launch_bounds__(256, 1)
         l_run *= factor;
       }
       const float safe = m_run == -INFINITY ? 0.f : m_run;
+      // P = exp2(s * scale * log2e - m) with packed f32x2 arithmetic; every
+      // other element pair goes through MUFU ex2, the rest through the
+      // FMA-pipe polynomial, and bf16 pairs are packed with integer rounding,
+      // so the special function unit stays below the tensor core's time.
       uint32_t pk[kBN / 2];
-      float sum = 0.f;
+      uint64_t sum2[2] = {ptx::f2pack(0.f, 0.f), ptx::f2pack(0.f, 0.f)};
+      if (!need_mask) {
+        const uint64_t sc2 = ptx::f2pack(qk_scale, qk_scale), ng2 = ptx::f2pack(-safe, -safe);
 #pragma unroll
-      for (int c = 0; c < kBN; c += 2) {
-        const float p0 = ptx::ex2(x[c] - safe), p1 = ptx::ex2(x[c + 1] - safe);
-        sum += p0 + p1;
-        pk[c / 2] = kBF16 ? ptx::pack_bf16(p0, p1) : ptx::pack_f16(p0, p1);
+        for (int c = 0; c < kBN; c += 2) {
+          const uint64_t x2 = ptx::fma2(ptx::f2pack(__uint_as_float(r[c]), __uint_as_float(r[c + 1])), sc2, ng2);
+          uint64_t p2;
+          if ((c & 2) == 0) {
+            float x0, x1;
+            ptx::f2unpack(x2, x0, x1);
+            p2 = ptx::f2pack(ptx::ex2(x0), ptx::ex2(x1));
+          } else {
+            p2 = ptx::exp2_poly2(x2);
+          }
+          sum2[(c >> 1) & 1] = ptx::add2(sum2[(c >> 1) & 1], p2);
+          float p0, p1;
+          ptx::f2unpack(p2, p0, p1);
+          pk[c / 2] = kBF16 ? ptx::pack_bf16_rhu(p0, p1) : ptx::pack_f16(p0, p1);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < kBN; c += 2) {
+          const int key = k0 + c;
+          float p0 = ptx::ex2(fmaf(__uint_as_float(r[c]), qk_scale, -safe));
+          float p1 = ptx::ex2(fmaf(__uint_as_float(r[c + 1]), qk_scale, -safe));
+          p0 = (key < kv_end && (int64_t)key <= lim) ? p0 : 0.f;
+          p1 = (key + 1 < kv_end && (int64_t)key + 1 <= lim) ? p1 : 0.f;
+          sum2[0] = ptx::add2(sum2[0], ptx::f2pack(p0, p1));
+          pk[c / 2] = kBF16 ? ptx::pack_bf16(p0, p1) : ptx::pack_f16(p0, p1);
+        }
       }
-      l_run += sum;
+      {
+        float a0, a1, b0, b1;
+        ptx::f2unpack(sum2[0], a0, a1);
+        ptx::f2unpack(sum2[1], b0, b1);
+        l_run += (a0 + a1) + (b0 + b1);
+      }
       // P buffer and O are free once P(j-1).V(j-1) has completed.
       if (j >= 1 && !__all_sync(0xffffffffu, wait_bar(&bars->o_done, (j - 1) & 1, args.fault, FAULT_FWD_O))) {
         ok = false;
@@ -367,6 +405,7 @@ bool tc_fwd_supported(const ts_attn_params& p) {
   if (p.dtype != TS_BF16 && p.dtype != TS_F16) return false;
   if (p.head_dim != p.value_dim || (p.head_dim != 64 && p.head_dim != 128)) return false;
   if (p.mask_kind != TS_MASK_NONE) return false;
+  if (!(p.scale > 0.0)) return false;  // the row max is taken on raw scores, then scaled
   if (!view_tma_ok(p.q) || !view_tma_ok(p.k) || !view_tma_ok(p.v)) return false;
   if (p.o.stride[3] != 1 || reinterpret_cast<uintptr_t>(p.o.data) % 16 || (p.o.stride[2] * 2) % 16 ||
       (p.o.stride[1] * 2) % 16 || (p.o.stride[0] * 2) % 16)

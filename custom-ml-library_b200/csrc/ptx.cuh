@@ -190,5 +190,64 @@ __device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
   return r;
 }
 
+// bf16 pair from two floats without the F2F conversion unit: round half up on
+// the bit pattern (add half an ulp of bf16, keep the upper 16 bits) and pick
+// both upper halves with one byte permute.  Differs from round-to-nearest-even
+// only on exact ties.  For finite, non-NaN inputs (softmax probabilities).
+__device__ __forceinline__ uint32_t pack_bf16_rhu(float lo, float hi) {
+  return __byte_perm(__float_as_uint(lo) + 0x8000u, __float_as_uint(hi) + 0x8000u, 0x7632);
+}
+
+// ------------------------- packed f32x2 arithmetic -------------------------
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair of floats on the FMA pipe (no MUFU): Cody-Waite style split
+// x = n + f with n = rint(x) (magic-constant rounding) and f in [-0.5, 0.5],
+// 2^f from a cubic fitted to 2^f on [-0.5, 0.5] by least squares in relative
+// error (max relative error 7.5e-5, below bf16 / f16 rounding of P), and 2^n
+// added to the exponent field.  Inputs are clamped to >= -126.
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
+  float x0, x1;
+  f2unpack(x, x0, x1);
+  x0 = fmaxf(x0, -126.f);
+  x1 = fmaxf(x1, -126.f);
+  const uint64_t xc = f2pack(x0, x1);
+  const uint64_t magic = f2pack(12582912.f, 12582912.f);      // 1.5 * 2^23
+  const uint64_t t = add2(xc, magic);                          // low bits hold rint(x)
+  const uint64_t n = add2(t, f2pack(-12582912.f, -12582912.f));
+  const uint64_t f = fma2(n, f2pack(-1.f, -1.f), xc);          // x - rint(x)
+  uint64_t q = fma2(f, f2pack(0.055171650f, 0.055171650f), f2pack(0.24261114f, 0.24261114f));
+  q = fma2(q, f, f2pack(0.69326097f, 0.69326097f));
+  q = fma2(q, f, f2pack(0.99992806f, 0.99992806f));
+  float q0, q1, t0, t1;
+  f2unpack(q, q0, q1);
+  f2unpack(t, t0, t1);
+  const uint32_t r0 = __float_as_uint(q0) + (__float_as_uint(t0) << 23);
+  const uint32_t r1 = __float_as_uint(q1) + (__float_as_uint(t1) << 23);
+  return f2pack(__uint_as_float(r0), __uint_as_float(r1));
+}
+
 }  // namespace ptx
 }  // namespace tsa

@@ -68,20 +68,32 @@ def stale() -> bool:
     return any(p.stat().st_mtime > built for p in deps)
 
 
+def _object_stale(src: Path) -> bool:
+    """An object is rebuilt when its source, any shared header, or the ABI header is newer."""
+    obj = BUILD / (src.stem + ".o")
+    if not obj.exists():
+        return True
+    deps = [src] + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
+    built = obj.stat().st_mtime
+    return any(p.stat().st_mtime > built for p in deps)
+
+
 def build(force: bool = False, verbose_ptxas: bool = False, jobs: int | None = None) -> Path:
     if not force and not stale():
         return LIB
     BUILD.mkdir(exist_ok=True)
     LIB_DIR.mkdir(exist_ok=True)
     srcs = sources()
-    jobs = jobs or min(len(srcs), os.cpu_count() or 4)
+    todo = [s for s in srcs if force or verbose_ptxas or _object_stale(s)]
+    jobs = jobs or max(1, min(len(todo), os.cpu_count() or 4))
     with concurrent.futures.ThreadPoolExecutor(jobs) as pool:
-        results = list(pool.map(lambda s: _compile(s, verbose_ptxas), srcs))
+        results = list(pool.map(lambda s: _compile(s, verbose_ptxas), todo))
     if verbose_ptxas:
-        for (_, log), src in zip(results, srcs):
+        for (_, log), src in zip(results, todo):
             sys.stderr.write(f"== {src.name}\n{log}")
+    objects = [BUILD / (s.stem + ".o") for s in srcs]
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *[str(o) for o, _ in results]]
+    cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *[str(o) for o in objects]]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stderr}")

@@ -37,6 +37,9 @@ TC_SHAPES = [
     (1, 2, 2, 100, 700, 64, 64, False, 0),
     (1, 1, 1, 1, 300, 128, 128, True, 299),   # one query at the end of a long key run
     (1, 2, 2, 1024, 1024, 64, 64, True, 0),
+    (1, 2, 2, 129, 129, 128, 128, True, 0),   # second query tile holds one row
+    (2, 2, 1, 255, 300, 64, 64, True, 45),    # partial second tile, GQA, offset
+    (1, 1, 1, 257, 1000, 128, 128, False, 0),
 ]
 
 
@@ -78,6 +81,16 @@ def test_forward_tcgen05(shape, name):
     q, k, v = _run(shape, name, seed=1)
     b, hq, hkv, tq, tk, d, dv, causal, off = shape
     assert engine.fwd_path(q, k, v, is_causal=causal, causal_offset=off) == "tcgen05"
+
+
+def test_negative_scale_routes_to_generic_path():
+    rng = np.random.default_rng(8)
+    q, k, v = (rounded(rng.standard_normal((1, 2, 130, 64)), "bfloat16") for _ in range(3))
+    tq_, tk_, tv_ = (to_cuda(x, "bfloat16") for x in (q, k, v))
+    assert engine.fwd_path(tq_, tk_, tv_, is_causal=True, scale=-0.125) == "simt"
+    out, _ = engine.forward(tq_, tk_, tv_, is_causal=True, scale=-0.125)
+    ref, _ = oracle_forward(q, k, v, is_causal=True, scale=-0.125)
+    assert_close(to_np(out), ref, "bfloat16", "negative scale")
 
 
 def test_fp32_takes_exact_path():
@@ -125,6 +138,27 @@ def test_kv_lens_matches_key_valid_mask():
     kv_lens = torch.tensor(lens, dtype=torch.int32, device="cuda")
     out, _ = engine.forward(*(to_cuda(x, "bfloat16") for x in (q, k, v)), is_causal=True, kv_lens=kv_lens)
     assert_close(to_np(out), ref, "bfloat16", "kv_lens tc")
+
+
+def test_kv_lens_shorter_than_queries_masks_leading_rows():
+    """Row with 60 valid keys and 200 queries: the first 140 queries see no key
+    (zero output, LSE -inf); the first 128-row tile has no key tile at all."""
+    rng = np.random.default_rng(21)
+    q = rounded(rng.standard_normal((2, 2, 200, 128)), "bfloat16")
+    k = rounded(rng.standard_normal((2, 2, 256, 128)), "bfloat16")
+    v = rounded(rng.standard_normal((2, 2, 256, 128)), "bfloat16")
+    lens = np.array([60, 256])
+    ref, ref_lse = oracle.decode_attention(q, k, v, lens)
+    kv_lens = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    tq_, tk_, tv_ = (to_cuda(x, "bfloat16") for x in (q, k, v))
+    assert engine.fwd_path(tq_, tk_, tv_, is_causal=True, kv_lens=kv_lens) == "tcgen05"
+    out, lse = engine.forward(tq_, tk_, tv_, is_causal=True, kv_lens=kv_lens)
+    torch.cuda.synchronize()
+    engine.check_device_status()
+    assert_close(to_np(out), ref, "bfloat16", "short kv_lens")
+    got = to_np(lse)
+    assert np.array_equal(np.isneginf(got), np.isneginf(ref_lse))
+    assert np.isneginf(got[0, :, :140]).all() and np.isfinite(got[0, :, 140:]).all()
 
 
 import oracle  # noqa: E402
