@@ -5,6 +5,7 @@
 #include "common.cuh"
 #include "decode.cuh"
 #include "kv_cache.cuh"
+#include "rope.cuh"
 #include "simt.cuh"
 #include "tc_bwd.cuh"
 #include "tc_fwd.cuh"
@@ -138,6 +139,29 @@ int ts_kv_append(const ts_kv_append_params* p, void* stream) {
   if (p->steps <= 0) return TS_ERR_CAPACITY;
   if (!p->positions && (p->position < 0 || p->position + p->steps > p->capacity)) return TS_ERR_CAPACITY;
   return from_cuda(tsa::kv_append(*p, as_stream(stream)));
+}
+
+int ts_rope(ts_view4 x, ts_view4 y, int32_t dtype, int32_t batch, int32_t heads, int32_t seq, int32_t channels,
+            int32_t rotary_dim, int64_t offset, const int32_t* positions, const float* inv_freq, int32_t inverse,
+            void* stream) {
+  if (!dtype_ok(dtype)) return TS_ERR_UNSUPPORTED;
+  if (!x.data || !y.data || !inv_freq || batch <= 0 || heads <= 0 || seq <= 0 || channels <= 0)
+    return TS_ERR_INVALID_ARGUMENT;
+  if (rotary_dim <= 0 || rotary_dim % 2 || rotary_dim > channels || offset < 0) return TS_ERR_INVALID_ARGUMENT;
+  return from_cuda(tsa::rope_apply(x, y, dtype, batch, heads, seq, channels, rotary_dim, offset, positions, inv_freq,
+                                   inverse, as_stream(stream)));
+}
+
+int ts_kv_append_rope(const ts_kv_append_params* p, const float* inv_freq, int32_t rotary_dim, void* stream) {
+  if (!p) return TS_ERR_INVALID_ARGUMENT;
+  if (!dtype_ok(p->src_dtype) || !dtype_ok(p->cache_dtype)) return TS_ERR_UNSUPPORTED;
+  if (p->batch <= 0 || p->heads <= 0 || p->head_dim <= 0 || p->value_dim <= 0 || p->capacity <= 0 || !inv_freq)
+    return TS_ERR_INVALID_ARGUMENT;
+  if (!p->key.data || !p->value.data || !p->key_cache.data || !p->value_cache.data) return TS_ERR_INVALID_ARGUMENT;
+  if (rotary_dim <= 0 || rotary_dim % 2 || rotary_dim > p->head_dim) return TS_ERR_INVALID_ARGUMENT;
+  if (p->steps <= 0) return TS_ERR_CAPACITY;
+  if (!p->positions && (p->position < 0 || p->position + p->steps > p->capacity)) return TS_ERR_CAPACITY;
+  return from_cuda(tsa::kv_append_rope(*p, inv_freq, rotary_dim, as_stream(stream)));
 }
 
 int ts_kv_reorder(ts_view4 src, ts_view4 dst, int32_t dtype, int32_t batch, int32_t heads, int32_t length,

@@ -108,6 +108,14 @@ SIGNATURES = {
     ),
     "ts_attn_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(AttnParams), ctypes.c_void_p]),
     "ts_kv_append": (ctypes.c_int, [ctypes.POINTER(KvAppendParams), ctypes.c_void_p]),
+    "ts_rope": (
+        ctypes.c_int,
+        [View4, View4, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+         ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p],
+    ),
+    "ts_kv_append_rope": (
+        ctypes.c_int, [ctypes.POINTER(KvAppendParams), ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p]
+    ),
     "ts_kv_reorder": (
         ctypes.c_int,
         [View4, View4, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,

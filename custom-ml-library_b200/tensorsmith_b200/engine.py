@@ -270,6 +270,62 @@ def kv_reorder(src, dst, index, length):
     )
 
 
+_INV_FREQ: dict = {}
+
+
+def rope_inv_freq(rotary_dim: int, base: float, device) -> torch.Tensor:
+    """inv_freq[i] = base^(-2i/rotary_dim) in fp32, evaluated as the reference
+    does it (float32 exponent array, nn/attention.py:274), cached per device."""
+    import numpy as np
+
+    key = (int(rotary_dim), float(base), str(device))
+    if key not in _INV_FREQ:
+        host = base ** (-np.arange(0, rotary_dim, 2).astype(np.float32) / rotary_dim)
+        _INV_FREQ[key] = torch.from_numpy(np.ascontiguousarray(host.astype(np.float32))).to(device)
+    return _INV_FREQ[key]
+
+
+def rope(x, *, offset=0, base=10000.0, rotary_dim=None, positions=None, inverse=False, out=None):
+    """Interleaved-pair rotary embedding of a [B, H, T, C] view at positions offset + t
+    (or positions[b] + t); ``inverse`` applies the inverse rotation (the VJP)."""
+    _require_cuda(x)
+    dim = x.shape[3] if rotary_dim is None else int(rotary_dim)
+    out = torch.empty_like(x) if out is None else out
+    inv = rope_inv_freq(dim, base, x.device)
+    pos = None
+    if positions is not None:
+        pos = positions if positions.dtype == torch.int32 else positions.to(torch.int32)
+    _lib.check(
+        _lib.lib().ts_rope(view4(x), view4(out), dtype_code(x.dtype), x.shape[0], x.shape[1], x.shape[2],
+                           x.shape[3], dim, int(offset), pos.data_ptr() if pos is not None else None,
+                           inv.data_ptr(), 1 if inverse else 0, _stream_handle(x.device)),
+        "ts_rope",
+    )
+    return out
+
+
+def kv_append_rope(key, value, key_cache, value_cache, *, position=0, positions=None, positions_out=None,
+                   base=10000.0, rotary_dim=None):
+    """kv_append with the keys rotated at their cache positions in the same pass."""
+    _require_cuda(key, value, key_cache, value_cache)
+    dim = key.shape[3] if rotary_dim is None else int(rotary_dim)
+    p = _lib.KvAppendParams()
+    p.key, p.value = view4(key), view4(value)
+    p.key_cache, p.value_cache = view4(key_cache), view4(value_cache)
+    p.src_dtype = dtype_code(key.dtype)
+    p.cache_dtype = dtype_code(key_cache.dtype)
+    if value.dtype != key.dtype or value_cache.dtype != key_cache.dtype:
+        raise TypeError("key/value and their caches must share a dtype each")
+    p.batch, p.heads, p.steps = key.shape[0], key.shape[1], key.shape[2]
+    p.head_dim, p.value_dim, p.capacity = key.shape[3], value.shape[3], key_cache.shape[2]
+    p.position = int(position)
+    p.positions = positions.data_ptr() if positions is not None else None
+    p.positions_out = positions_out.data_ptr() if positions_out is not None else None
+    inv = rope_inv_freq(dim, base, key.device)
+    _lib.check(_lib.lib().ts_kv_append_rope(ctypes.byref(p), inv.data_ptr(), dim, _stream_handle(key.device)),
+               "ts_kv_append_rope")
+
+
 def device_status(device=None) -> tuple[int, int]:
     """(status, site) of the device fault word; clears it.  Synchronises the stream."""
     device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)

@@ -1,4 +1,4 @@
 """tensorsmith ``nn`` attention surface served by the B200 engine."""
 
-from .attention import scaled_dot_product_attention  # noqa: F401
+from .attention import rotary_embedding, scaled_dot_product_attention  # noqa: F401
 from .cache import KVCache  # noqa: F401

@@ -103,3 +103,35 @@ def scaled_dot_product_attention(
         return dq, dk, dv
 
     return Tensor._from_op(output, (query, key, value), backward, "sdpa_" + selected)
+
+
+def rotary_embedding(input: Tensor, offset: int = 0, base: float = 10000.0, rotary_dim: int | None = None) -> Tensor:
+    """Interleaved-pair RoPE for [..., sequence, channels], with inverse-rotation VJP.
+
+    Signature, validation and semantics of nn/attention.py:255-296; computed by
+    the engine's rope kernel (per-operation rounding in the input dtype)."""
+    if input.ndim < 2:
+        raise ValueError("RoPE requires at least sequence and channel dimensions")
+    dim = input.shape[-1] if rotary_dim is None else rotary_dim
+    if (
+        dim <= 0
+        or dim % 2
+        or dim > input.shape[-1]
+        or offset < 0
+        or base <= 0
+        or not math.isfinite(base)
+    ):
+        raise ValueError("RoPE requires a positive even rotary dimension and valid positions/base")
+    if input.device.type != "cuda":
+        raise ValueError("the B200 attention engine runs on cuda tensors")
+    raw = input._data
+    shape = raw.shape
+    x4 = raw.reshape((-1,) + tuple(shape[-2:]))[None] if raw.dim() != 4 else raw
+    out = engine.rope(x4, offset=offset, base=base, rotary_dim=dim).reshape(shape)
+
+    def backward(g):
+        g4 = g.reshape((-1,) + tuple(shape[-2:]))[None] if g.dim() != 4 else g
+        return (engine.rope(g4.contiguous() if not g4.is_contiguous() else g4, offset=offset, base=base,
+                            rotary_dim=dim, inverse=True).reshape(shape),)
+
+    return Tensor._from_op(out, (input,), backward, "rope")

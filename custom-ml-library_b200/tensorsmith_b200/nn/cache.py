@@ -100,6 +100,42 @@ class KVCache:
             self.length = int(self._host_lens.max())
         return self.get()
 
+    def append_rotary(self, key: Tensor, value: Tensor, *, base: float = 10000.0,
+                      rotary_dim: int | None = None) -> tuple[Tensor, Tensor]:
+        """``append(rotary_embedding(key, self.length), value)`` in one kernel.
+
+        The attention module rotates keys at their cache positions and then
+        appends them (nn/transformer.py:139-142, nn/cache.py:54-86); this
+        writes the rotated keys straight into the cache (per-row positions
+        when the cache has ragged lengths)."""
+        dim = self.head_dim if rotary_dim is None else rotary_dim
+        if dim <= 0 or dim % 2 or dim > self.head_dim or base <= 0 or not np.isfinite(base):
+            raise ValueError("RoPE requires a positive even rotary dimension and valid positions/base")
+        if key.device != self.device or value.device != self.device:
+            raise ValueError("cache and key/value tensors must be on the same device")
+        if is_grad_enabled() and (key.requires_grad or value.requires_grad):
+            raise RuntimeError("KVCache is inference-only; use no_grad() for differentiable inputs")
+        prefix = (self.batch_size, self.num_heads)
+        if key.ndim != 4 or key.shape[:2] != prefix or key.shape[-1] != self.head_dim:
+            raise ValueError("key shape does not match cache configuration")
+        if value.shape != key.shape[:3] + (self.value_dim,):
+            raise ValueError("value shape does not match cache configuration")
+        steps = key.shape[2]
+        top = self.length if self._host_lens is None else int(self._host_lens.max())
+        if steps == 0 or top + steps > self.max_seq_len:
+            raise ValueError(f"cache capacity {self.max_seq_len} exceeded or empty append")
+        if self._host_lens is None:
+            engine.kv_append_rope(key._data, value._data, self._keys, self._values, position=self.length,
+                                  base=base, rotary_dim=dim)
+            self.length += steps
+        else:
+            engine.kv_append_rope(key._data, value._data, self._keys, self._values, positions=self._lens,
+                                  positions_out=self._lens_next, base=base, rotary_dim=dim)
+            self._lens, self._lens_next = self._lens_next, self._lens
+            self._host_lens = self._host_lens + steps
+            self.length = int(self._host_lens.max())
+        return self.get()
+
     def get(self) -> tuple[Tensor, Tensor]:
         keys = self._keys[:, :, : self.length]
         values = self._values[:, :, : self.length]

@@ -155,6 +155,21 @@ TS_ATTN_API int ts_attn_decode(const ts_attn_params* params, void* workspace, si
 /* KVCache.append slice write (nn/cache.py:54-86, unquantized storage). */
 TS_ATTN_API int ts_kv_append(const ts_kv_append_params* params, void* stream);
 
+/* Interleaved-pair rotary embedding of nn/attention.py:255-296 on a
+ * [B, H, T, C] view: y = rope(x) at positions (positions[b] or offset) + t,
+ * first rotary_dim (even) channels, inv_freq[i] = base^(-2i/rotary_dim) as
+ * fp32 (rotary_dim/2 entries, device).  inverse != 0 applies the inverse
+ * rotation (the VJP of :287-293).  y may alias x. */
+TS_ATTN_API int ts_rope(ts_view4 x, ts_view4 y, int32_t dtype, int32_t batch, int32_t heads, int32_t seq,
+                        int32_t channels, int32_t rotary_dim, int64_t offset, const int32_t* positions,
+                        const float* inv_freq, int32_t inverse, void* stream);
+
+/* KVCache.append with the key rotation of the attention module fused into the
+ * write (nn/transformer.py:139-142 followed by nn/cache.py:54-86): keys are
+ * rotated at their cache positions, values copied. */
+TS_ATTN_API int ts_kv_append_rope(const ts_kv_append_params* params, const float* inv_freq, int32_t rotary_dim,
+                                  void* stream);
+
 /* KVCache.reorder batch gather (nn/cache.py:110-123): dst[b] = src[index[b]].
  * src and dst must not overlap. */
 TS_ATTN_API int ts_kv_reorder(ts_view4 src, ts_view4 dst, int32_t dtype, int32_t batch, int32_t heads,
