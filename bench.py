@@ -47,6 +47,8 @@ WORKLOADS = {
     "c3": dict(batch=8, heads=16, head_dim=128, prefill=4096),
     # fp16 KV-cache decode, ragged lengths U[1024, 8192], 256 steps with append
     "c4": dict(batch=64, heads=32, head_dim=128, min_len=1024, max_len=8192, decode_steps=256),
+    # config 3 with the int8 KV cache (KVCache(quantized=True)): quantising append + fused-dequant decode
+    "c4q": dict(batch=64, heads=32, head_dim=128, min_len=1024, max_len=8192, decode_steps=256),
 }
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -207,6 +209,11 @@ def run_reference(args, rank: int, world: int):
     if rank != 0:
         return
     cfg = WORKLOADS[args.workload]
+    if "prefill" not in cfg:
+        print(json.dumps({"impl": "reference", "workload": args.workload,
+                          "unavailable": "the reference arm times the prefill+decode workloads (c5, small, c3); "
+                                         "the decode-only configs report the oracle port as cpu_baseline"}))
+        return
     budget = max(2.0, min(args.cpu_seconds, 8.0))
     values, decode = [], []
     for step in range(args.warmup + args.steps):
@@ -570,14 +577,15 @@ def cpu_c3_baseline(cfg, budget_s):
                                       f"one (b,h) slice vs T={T} keys, median of {len(times)} reps"}
 
 
-def run_c4(args):
-    """fp16 KV-cache decode, B=64 H=32 D=128, ragged lengths, 256 steps with append."""
+def run_c4(args, quantized=False):
+    """fp16 KV-cache decode, B=64 H=32 D=128, ragged lengths, 256 steps with append (BASELINE config 3);
+    ``quantized``: the same steps over an int8 cache (quantising append + fused-dequant decode)."""
     import numpy as np
     import torch
 
     from tensorsmith_b200 import engine
 
-    cfg = WORKLOADS["c4"]
+    cfg = WORKLOADS["c4q" if quantized else "c4"]
     B, H, D, S = cfg["batch"], cfg["heads"], cfg["head_dim"], cfg["decode_steps"]
     cap = cfg["max_len"] + S
     dev = torch.device("cuda", 0)
@@ -590,8 +598,19 @@ def run_c4(args):
     out = torch.empty(S, B, H, 1, D, dtype=torch.float16, device=dev)
     start_lens = torch.tensor(lens0, dtype=torch.int32, device=dev)
     lens = [torch.empty_like(start_lens), torch.empty_like(start_lens)]
-    ws = torch.empty(max(16, engine.decode_workspace_bytes(qn[0], kc, vc, is_causal=True, kv_lens=start_lens)),
-                     dtype=torch.uint8, device=dev)
+    if quantized:
+        # Quantise the synthetic fp16 prefix once (the same kernel a prefill append runs).
+        k8 = torch.empty(B, H, cap, D, dtype=torch.int8, device=dev)
+        v8 = torch.empty_like(k8)
+        ks = torch.ones(B, H, cap, dtype=torch.float32, device=dev)
+        vs = torch.ones_like(ks)
+        engine.kv_append_int8(kc, vc, k8, v8, ks, vs, compute_dtype=torch.float16, position=0)
+        del kc, vc
+        kc, vc = k8, v8
+        need = engine.decode_int8_workspace_bytes(qn[0], kc, vc, is_causal=True, kv_lens=start_lens)
+    else:
+        need = engine.decode_workspace_bytes(qn[0], kc, vc, is_causal=True, kv_lens=start_lens)
+    ws = torch.empty(max(16, need), dtype=torch.uint8, device=dev)
     splits = ws.numel() > 16
 
     def step(ev):
@@ -599,13 +618,19 @@ def run_c4(args):
         ev[0].record()
         for s in range(S):
             cur, nxt = lens[s & 1], lens[(s + 1) & 1]
-            engine.kv_append(kn[s], vn[s], kc, vc, positions=cur, positions_out=nxt)
-            engine.decode(qn[s], kc, vc, is_causal=True, kv_lens=nxt, out=out[s], workspace=ws)
+            if quantized:
+                engine.kv_append_int8(kn[s], vn[s], kc, vc, ks, vs, compute_dtype=torch.float16, positions=cur,
+                                      positions_out=nxt)
+                engine.decode_int8(qn[s], kc, vc, ks, vs, is_causal=True, kv_lens=nxt, out=out[s], workspace=ws)
+            else:
+                engine.kv_append(kn[s], vn[s], kc, vc, positions=cur, positions_out=nxt)
+                engine.decode(qn[s], kc, vc, is_causal=True, kv_lens=nxt, out=out[s], workspace=ws)
         ev[1].record()
 
     evs, step_ms, clocks = _timed(args, step, 2)
     dec = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
-    kv_bytes = float(sum(2 * H * D * 2 * (lens0 + s + 1).sum() for s in range(S)))
+    row_bytes = D + 4 if quantized else 2 * D  # int8 row + fp32 scale, or fp16 row
+    kv_bytes = float(sum(2 * H * row_bytes * (lens0 + s + 1).sum() for s in range(S)))
     peaks, src = load_peaks()
     gbs = kv_bytes / (dec / 1e3) / 1e9
     tokens = B * S / (dec / 1e3)
@@ -613,15 +638,20 @@ def run_c4(args):
         "metric": METRIC, "value": tokens, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": f"c4: fp16 KV-cache decode B={B} H={H} D={D}, lengths U[{cfg['min_len']},"
+        "config": {"workload": (f"c4q: fp16 decode over an int8 KV cache (fp32 scale per token/head) "
+                                if quantized else "c4: fp16 KV-cache decode ")
+                               + f"B={B} H={H} D={D}, lengths U[{cfg['min_len']},"
                                f"{cfg['max_len']}] per row, {S} decode steps each appending one token",
-                   "l2": "cache 8.9 GB, larger than L2"},
+                   "l2": "cache 4.6 GB, larger than L2" if quantized else "cache 8.9 GB, larger than L2"},
         "decode": {"tokens_per_s": tokens, "hbm_gbs": gbs, "ms_per_token_step": dec / S,
                    "frac_of_measured_hbm": gbs / peaks["hbm_gbs"], "frac_of_nominal_8000": gbs / 8000.0},
-        "roofline": {"bound": "hbm", "kernel": "decode step (kv_append + decode_split + combine)", "achieved": gbs,
-                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"],
+        "roofline": {"bound": "hbm",
+                     "kernel": ("decode step (kv_append_int8 + decode_int8 + combine)" if quantized
+                                else "decode step (kv_append + decode_split + combine)"),
+                     "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"],
                      "peak_source": f"{src} hbm_gbs", "traffic": None,
-                     "algorithmic": "sum_b 2*H*L_b*D*2 bytes (K+V fp16 read) per step"},
+                     "algorithmic": ("sum_b 2*H*L_b*(D+4) bytes (int8 K+V rows and fp32 scales read) per step"
+                                     if quantized else "sum_b 2*H*L_b*D*2 bytes (K+V fp16 read) per step")},
         "gpu_launches": S * (2 + (1 if splits else 0)) * args.steps,
         "clocks": clocks,
     }
@@ -654,10 +684,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if args.workload in ("c3", "c4"):
+        if args.workload in ("c3", "c4", "c4q"):
             if world > 1:
                 raise SystemExit("the c3 / c4 parity configs run on one GPU; c5 is the multi-GPU workload")
-            result = (run_c3 if args.workload == "c3" else run_c4)(args)
+            result = run_c3(args) if args.workload == "c3" else run_c4(args, quantized=args.workload == "c4q")
         else:
             result = run_engine(args, rank, world, local_rank)
         if rank == 0 and result is not None:

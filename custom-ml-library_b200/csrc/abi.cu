@@ -4,6 +4,7 @@
 
 #include "common.cuh"
 #include "decode.cuh"
+#include "int8.cuh"
 #include "kv_cache.cuh"
 #include "rope.cuh"
 #include "simt.cuh"
@@ -166,10 +167,49 @@ int ts_kv_append_rope(const ts_kv_append_params* p, const float* inv_freq, int32
 
 int ts_kv_reorder(ts_view4 src, ts_view4 dst, int32_t dtype, int32_t batch, int32_t heads, int32_t length,
                   int32_t channels, const int32_t* index, void* stream) {
-  if (!dtype_ok(dtype)) return TS_ERR_UNSUPPORTED;
+  if (!dtype_ok(dtype) && dtype != TS_I8) return TS_ERR_UNSUPPORTED;
   if (!src.data || !dst.data || !index || batch <= 0 || heads <= 0 || length < 0 || channels <= 0)
     return TS_ERR_INVALID_ARGUMENT;
   return from_cuda(tsa::kv_reorder(src, dst, dtype, batch, heads, length, channels, index, as_stream(stream)));
+}
+
+int ts_kv_append_int8(const ts_kv_append_params* p, float* key_scales, float* value_scales, void* stream) {
+  if (!p) return TS_ERR_INVALID_ARGUMENT;
+  if (!dtype_ok(p->src_dtype) || !dtype_ok(p->cache_dtype)) return TS_ERR_UNSUPPORTED;
+  if (p->batch <= 0 || p->heads <= 0 || p->head_dim <= 0 || p->value_dim <= 0 || p->capacity <= 0)
+    return TS_ERR_INVALID_ARGUMENT;
+  if (!p->key.data || !p->value.data || !p->key_cache.data || !p->value_cache.data || !key_scales || !value_scales)
+    return TS_ERR_INVALID_ARGUMENT;
+  if (p->steps <= 0) return TS_ERR_CAPACITY;
+  if (!p->positions && (p->position < 0 || p->position + p->steps > p->capacity)) return TS_ERR_CAPACITY;
+  return from_cuda(tsa::kv_append_int8(*p, key_scales, value_scales, as_stream(stream)));
+}
+
+int ts_kv_dequant_int8(ts_view4 src, const float* scales, int64_t scale_capacity, ts_view4 dst, int32_t dtype,
+                       int32_t batch, int32_t heads, int32_t length, int32_t channels, void* stream) {
+  if (!dtype_ok(dtype)) return TS_ERR_UNSUPPORTED;
+  if (!src.data || !dst.data || !scales || batch <= 0 || heads <= 0 || length < 0 || channels <= 0 ||
+      scale_capacity < length)
+    return TS_ERR_INVALID_ARGUMENT;
+  return from_cuda(tsa::kv_dequant_int8(src, scales, scale_capacity, dst, dtype, batch, heads, length, channels,
+                                        as_stream(stream)));
+}
+
+size_t ts_attn_decode_int8_workspace_size(const ts_attn_params* p) {
+  if (check_params(p) != TS_OK || !tsa::decode_int8_supported(*p)) return 0;
+  return tsa::decode_int8_workspace(*p);
+}
+
+int ts_attn_decode_int8(const ts_attn_params* p, const float* key_scales, const float* value_scales,
+                        int64_t scale_capacity, void* workspace, size_t workspace_bytes, void* stream) {
+  const int st = check_params(p);
+  if (st != TS_OK) return st;
+  if (!key_scales || !value_scales || scale_capacity < p->kv_len) return TS_ERR_INVALID_ARGUMENT;
+  if (!tsa::decode_int8_supported(*p)) return TS_ERR_UNSUPPORTED;
+  const size_t need = tsa::decode_int8_workspace(*p);
+  if (need && (!workspace || workspace_bytes < need)) return TS_ERR_WORKSPACE;
+  return from_cuda(tsa::decode_int8_forward(*p, key_scales, value_scales, scale_capacity, workspace,
+                                            workspace_bytes, fault_ptr(), as_stream(stream)));
 }
 
 int ts_attn_device_status(void* stream, uint32_t* info) {

@@ -137,6 +137,7 @@ cudaError_t kv_reorder(const ts_view4& src, const ts_view4& dst, int dtype, int 
     case TS_BF16:
       kv_reorder_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(src, dst, heads, length, channels, index);
       break;
+    case TS_I8: kv_reorder_kernel<int8_t><<<grid, 128, 0, st>>>(src, dst, heads, length, channels, index); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

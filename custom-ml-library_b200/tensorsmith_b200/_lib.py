@@ -16,6 +16,7 @@ LIB_PATH = Path(__file__).resolve().parent / "lib" / "libts_attn.so"
 
 # ts_dtype
 F32, F16, BF16, F64 = 0, 1, 2, 3
+I8 = 4  # storage type of the int8 KV cache only
 # ts_mask_kind
 MASK_NONE, MASK_BOOL, MASK_ADD_F32 = 0, 1, 2
 # ts_fwd_path
@@ -120,6 +121,20 @@ SIGNATURES = {
         ctypes.c_int,
         [View4, View4, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
          ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p],
+    ),
+    "ts_kv_append_int8": (
+        ctypes.c_int, [ctypes.POINTER(KvAppendParams), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    ),
+    "ts_kv_dequant_int8": (
+        ctypes.c_int,
+        [View4, ctypes.c_void_p, ctypes.c_int64, View4, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+         ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p],
+    ),
+    "ts_attn_decode_int8_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(AttnParams)]),
+    "ts_attn_decode_int8": (
+        ctypes.c_int,
+        [ctypes.POINTER(AttnParams), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+         ctypes.c_size_t, ctypes.c_void_p],
     ),
     "ts_attn_device_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
 }

@@ -258,16 +258,105 @@ def kv_append(key, value, key_cache, value_cache, *, position=0, positions=None,
     _lib.check(_lib.lib().ts_kv_append(ctypes.byref(p), _stream_handle(key.device)), "ts_kv_append")
 
 
+def _storage_code(dtype: torch.dtype) -> int:
+    return _lib.I8 if dtype == torch.int8 else dtype_code(dtype)
+
+
 def kv_reorder(src, dst, index, length):
-    """dst[b, :, :length] = src[index[b], :, :length] (beam reorder)."""
+    """dst[b, :, :length] = src[index[b], :, :length] (beam reorder; int8 storage too)."""
     _require_cuda(src, dst, index)
     idx = index if index.dtype == torch.int32 else index.to(torch.int32)
     _lib.check(
-        _lib.lib().ts_kv_reorder(view4(src), view4(dst), dtype_code(src.dtype), src.shape[0],
+        _lib.lib().ts_kv_reorder(view4(src), view4(dst), _storage_code(src.dtype), src.shape[0],
                                  src.shape[1], int(length), src.shape[3], idx.data_ptr(),
                                  _stream_handle(src.device)),
         "ts_kv_reorder",
     )
+
+
+def _check_int8_cache(cache, scales):
+    if cache.dtype != torch.int8 or cache.dim() != 4:
+        raise TypeError("int8 cache storage must be an int8 [B, H, capacity, C] tensor")
+    if scales.dtype != torch.float32 or not scales.is_contiguous() or scales.numel() != cache.shape[0] * cache.shape[1] * cache.shape[2]:
+        raise ValueError("int8 cache scales must be contiguous fp32 [B, H, capacity(, 1)]")
+
+
+def kv_append_int8(key, value, key_cache, value_cache, key_scales, value_scales, *, compute_dtype,
+                   position=0, positions=None, positions_out=None):
+    """Quantising append (nn/cache.py:70-82): rows rounded to ``compute_dtype``, then
+    symmetric int8 with one fp32 scale per (row, head, token) written to the scale arrays."""
+    _require_cuda(key, value, key_cache, value_cache, key_scales, value_scales)
+    _check_int8_cache(key_cache, key_scales)
+    _check_int8_cache(value_cache, value_scales)
+    if value.dtype != key.dtype:
+        raise TypeError("key/value must share a dtype")
+    p = _lib.KvAppendParams()
+    p.key, p.value = view4(key), view4(value)
+    p.key_cache, p.value_cache = view4(key_cache), view4(value_cache)
+    p.src_dtype = dtype_code(key.dtype)
+    p.cache_dtype = dtype_code(compute_dtype)
+    p.batch, p.heads, p.steps = key.shape[0], key.shape[1], key.shape[2]
+    p.head_dim, p.value_dim, p.capacity = key.shape[3], value.shape[3], key_cache.shape[2]
+    p.position = int(position)
+    p.positions = positions.data_ptr() if positions is not None else None
+    p.positions_out = positions_out.data_ptr() if positions_out is not None else None
+    _lib.check(_lib.lib().ts_kv_append_int8(ctypes.byref(p), key_scales.data_ptr(), value_scales.data_ptr(),
+                                            _stream_handle(key.device)), "ts_kv_append_int8")
+
+
+def kv_dequant_int8(src, scales, out, length):
+    """out[:, :, :length] = dtype(float(src) * scale) for an int8 cache (nn/cache.py:91-99)."""
+    _require_cuda(src, scales, out)
+    _check_int8_cache(src, scales)
+    _lib.check(
+        _lib.lib().ts_kv_dequant_int8(view4(src), scales.data_ptr(), src.shape[2], view4(out),
+                                      dtype_code(out.dtype), src.shape[0], src.shape[1], int(length),
+                                      src.shape[3], _stream_handle(src.device)),
+        "ts_kv_dequant_int8",
+    )
+
+
+def _int8_params(q, k8, v8, out, lse, kw):
+    _require_cuda(q, k8, v8)
+    if k8.dtype != torch.int8 or v8.dtype != torch.int8:
+        raise TypeError("int8 decode expects int8 key/value storage")
+    dtype_code(q.dtype)
+    return make_params(q, k8, v8, out, lse, **kw)
+
+
+def decode_int8_workspace_bytes(q, k8, v8, **kw) -> int:
+    o = torch.empty((q.shape[0], q.shape[1], q.shape[2], v8.shape[3]), dtype=q.dtype, device=q.device)
+    p, keep = _int8_params(q, k8, v8, o, None, kw)
+    return int(_lib.lib().ts_attn_decode_int8_workspace_size(ctypes.byref(p)))
+
+
+def decode_int8(q, k8, v8, key_scales, value_scales, *, is_causal=True, scale=None, causal_offset=0,
+                kv_lens=None, need_lse=False, out=None, lse=None, workspace=None):
+    """Split-K decode reading an int8 cache directly (dequantisation fused into the scores
+    and the P.V sum).  ``k8``/``v8`` are the first ``kv_len`` positions of the int8 storage;
+    ``key_scales``/``value_scales`` the full contiguous [B, H, capacity] scale arrays."""
+    _require_cuda(key_scales, value_scales)
+    b, hq, tq, _ = q.shape
+    if out is None:
+        out = torch.empty((b, hq, tq, v8.shape[3]), dtype=q.dtype, device=q.device)
+    if need_lse and lse is None:
+        lse = torch.empty((b, hq, tq), dtype=lse_dtype(q.dtype), device=q.device)
+    kw = dict(is_causal=is_causal, scale=scale, causal_offset=causal_offset, kv_lens=kv_lens)
+    p, keep = _int8_params(q, k8, v8, out, lse if need_lse else None, kw)
+    cap = key_scales.numel() // (k8.shape[0] * k8.shape[1])
+    if (key_scales.dtype != torch.float32 or value_scales.dtype != torch.float32 or not key_scales.is_contiguous()
+            or not value_scales.is_contiguous() or value_scales.numel() != key_scales.numel()):
+        raise ValueError("int8 cache scales must be contiguous fp32 [B, H, capacity(, 1)]")
+    handle = _lib.lib()
+    need = int(handle.ts_attn_decode_int8_workspace_size(ctypes.byref(p)))
+    if need and (workspace is None or workspace.numel() * workspace.element_size() < need):
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    ws_ptr = workspace.data_ptr() if (need and workspace is not None) else None
+    ws_bytes = workspace.numel() * workspace.element_size() if (need and workspace is not None) else 0
+    _lib.check(handle.ts_attn_decode_int8(ctypes.byref(p), key_scales.data_ptr(), value_scales.data_ptr(), cap,
+                                          ws_ptr, ws_bytes, _stream_handle(q.device)), "ts_attn_decode_int8")
+    del keep
+    return out, (lse if need_lse else None)
 
 
 _INV_FREQ: dict = {}

@@ -7,6 +7,10 @@ tensor (the reference layout), zero-initialised, so a decode kernel may read a
 whole 128-key tile past a row's valid length without meeting non-finite
 values.
 
+``quantized=True`` stores symmetric int8 rows with one fp32 scale per token
+and head (nn/cache.py:47-52, 70-82); ``get`` returns dequantised copies as the
+reference does, and ``attend`` decodes straight from the int8 rows.
+
 Engine extension for ragged batches (the reference expresses them with a
 key-valid mask over a padded cache, docs/transformers.md:52-55): after
 ``set_lengths(lengths)`` every row has its own valid length; ``append``
@@ -60,14 +64,15 @@ class KVCache:
         self.dtype = _torch_dtype(dtype)
         if not self.dtype.is_floating_point:
             raise TypeError("cache compute dtype must be floating point")
-        if quantized:
-            raise NotImplementedError("int8 KV storage is not implemented by the B200 engine")
-        self.quantized = False
+        self.quantized = bool(quantized)
         self.length = 0
         dev = torch.device("cuda", self.device.index)
         shape = (batch_size, num_heads, max_seq_len)
-        self._keys = torch.zeros(shape + (head_dim,), dtype=self.dtype, device=dev)
-        self._values = torch.zeros(shape + (self.value_dim,), dtype=self.dtype, device=dev)
+        store = torch.int8 if self.quantized else self.dtype
+        self._keys = torch.zeros(shape + (head_dim,), dtype=store, device=dev)
+        self._values = torch.zeros(shape + (self.value_dim,), dtype=store, device=dev)
+        self._key_scales = torch.ones(shape + (1,), dtype=torch.float32, device=dev) if self.quantized else None
+        self._value_scales = torch.ones(shape + (1,), dtype=torch.float32, device=dev) if self.quantized else None
         self._host_lens: np.ndarray | None = None
         self._lens: torch.Tensor | None = None
         self._lens_next: torch.Tensor | None = None
@@ -89,16 +94,27 @@ class KVCache:
         stop = top + steps
         if steps == 0 or stop > self.max_seq_len:
             raise ValueError(f"cache capacity {self.max_seq_len} exceeded or empty append")
-        if self._host_lens is None:
-            engine.kv_append(key._data, value._data, self._keys, self._values, position=self.length)
-            self.length = stop
+        self._write(key._data, value._data, steps)
+        return self.get()
+
+    def _write(self, key, value, steps: int) -> None:
+        """One append kernel: plain copy/cast, or quantising for int8 storage."""
+        where = {"position": self.length} if self._host_lens is None else {
+            "positions": self._lens, "positions_out": self._lens_next}
+        if self.quantized:
+            engine.kv_append_int8(key, value, self._keys, self._values, self._key_scales, self._value_scales,
+                                  compute_dtype=self.dtype, **where)
         else:
-            engine.kv_append(key._data, value._data, self._keys, self._values, positions=self._lens,
-                             positions_out=self._lens_next)
+            engine.kv_append(key, value, self._keys, self._values, **where)
+        self._advance(steps)
+
+    def _advance(self, steps: int) -> None:
+        if self._host_lens is None:
+            self.length += steps
+        else:
             self._lens, self._lens_next = self._lens_next, self._lens
             self._host_lens = self._host_lens + steps
             self.length = int(self._host_lens.max())
-        return self.get()
 
     def append_rotary(self, key: Tensor, value: Tensor, *, base: float = 10000.0,
                       rotary_dim: int | None = None) -> tuple[Tensor, Tensor]:
@@ -124,22 +140,66 @@ class KVCache:
         top = self.length if self._host_lens is None else int(self._host_lens.max())
         if steps == 0 or top + steps > self.max_seq_len:
             raise ValueError(f"cache capacity {self.max_seq_len} exceeded or empty append")
-        if self._host_lens is None:
-            engine.kv_append_rope(key._data, value._data, self._keys, self._values, position=self.length,
-                                  base=base, rotary_dim=dim)
-            self.length += steps
-        else:
-            engine.kv_append_rope(key._data, value._data, self._keys, self._values, positions=self._lens,
-                                  positions_out=self._lens_next, base=base, rotary_dim=dim)
-            self._lens, self._lens_next = self._lens_next, self._lens
-            self._host_lens = self._host_lens + steps
-            self.length = int(self._host_lens.max())
+        if self.quantized:
+            # Rotate, then quantise (the scale of a row depends on its rotated values).
+            rotated = engine.rope(key._data, offset=self.length if self._host_lens is None else 0, base=base,
+                                  rotary_dim=dim, positions=self._lens)
+            self._write(rotated, value._data, steps)
+            return self.get()
+        where = {"position": self.length} if self._host_lens is None else {
+            "positions": self._lens, "positions_out": self._lens_next}
+        engine.kv_append_rope(key._data, value._data, self._keys, self._values, base=base, rotary_dim=dim, **where)
+        self._advance(steps)
         return self.get()
 
     def get(self) -> tuple[Tensor, Tensor]:
         keys = self._keys[:, :, : self.length]
         values = self._values[:, :, : self.length]
+        if self.quantized:
+            # Dequantised copies of the active prefix (nn/cache.py:91-99).
+            b, h, n = self.batch_size, self.num_heads, self.length
+            keys = torch.empty((b, h, n, self.head_dim), dtype=self.dtype, device=self._keys.device)
+            values = torch.empty((b, h, n, self.value_dim), dtype=self.dtype, device=self._keys.device)
+            engine.kv_dequant_int8(self._keys, self._key_scales, keys, n)
+            engine.kv_dequant_int8(self._values, self._value_scales, values, n)
         return Tensor(keys, device=self.device), Tensor(values, device=self.device)
+
+    def attend(self, query: Tensor, *, scale: float | None = None, causal_offset: int | None = None) -> Tensor:
+        """Causal attention of ``query`` [B, Hq, Tq, D] (the newest Tq cached tokens)
+        over the cache, without materialising dequantised keys (engine extension).
+
+        Equals ``scaled_dot_product_attention(query, *self.get(), is_causal=True,
+        causal_offset=length - Tq, enable_gqa=True)`` (nn/transformer.py:143-154),
+        per-row lengths included.  An int8 cache runs the fused-dequant decode
+        kernel; shapes outside it dequantise and run the prefill kernels."""
+        if query.ndim != 4 or query.shape[0] != self.batch_size or query.shape[-1] != self.head_dim:
+            raise ValueError("query shape does not match cache configuration")
+        if query.shape[1] % self.num_heads or query.device != self.device:
+            raise ValueError("query heads must be a multiple of the cache heads, on the cache device")
+        if query.dtype != self.dtype:
+            raise TypeError("query dtype must be the cache compute dtype")
+        n, tq = self.length, query.shape[2]
+        if n == 0 or tq > n:
+            raise ValueError("the cache must already hold the query tokens")
+        offset = n - tq if causal_offset is None else int(causal_offset)
+        kw = dict(is_causal=True, scale=scale, causal_offset=offset, kv_lens=self._lens)
+        q = query._data
+        if self.quantized:
+            try:
+                out, _ = engine.decode_int8(q, self._keys[:, :, :n], self._values[:, :, :n], self._key_scales,
+                                            self._value_scales, **kw)
+                return Tensor(out, device=self.device)
+            except engine._lib.EngineError as error:
+                if error.status != engine._lib.ERR_UNSUPPORTED:
+                    raise
+            keys, values = (t._data for t in self.get())
+        else:
+            keys, values = self._keys[:, :, :n], self._values[:, :, :n]
+        if (query.shape[1] // self.num_heads) * tq <= engine.DECODE_MAX_ROWS:
+            out, _ = engine.decode(q, keys, values, **kw)
+        else:
+            out, _ = engine.forward(q, keys, values, need_lse=False, **kw)
+        return Tensor(out, device=self.device)
 
     def reset(self) -> None:
         """Reuse the allocation; future appends overwrite old entries."""
@@ -168,17 +228,26 @@ class KVCache:
         engine.kv_reorder(self._keys, keys, order, self.max_seq_len)
         engine.kv_reorder(self._values, values, order, self.max_seq_len)
         self._keys, self._values = keys, values
+        if self.quantized:
+            ks, vs = torch.empty_like(self._key_scales), torch.empty_like(self._value_scales)
+            engine.kv_reorder(self._key_scales, ks, order, self.max_seq_len)
+            engine.kv_reorder(self._value_scales, vs, order, self.max_seq_len)
+            self._key_scales, self._value_scales = ks, vs
         if self._host_lens is not None:
             self.set_lengths(self._host_lens[host])
 
     @property
     def storage(self) -> tuple:
         """Raw persistent arrays (keys, values, key scales, value scales)."""
-        return self._keys, self._values, None, None
+        return self._keys, self._values, self._key_scales, self._value_scales
 
     @property
     def memory_bytes(self) -> int:
-        return sum(t.numel() * t.element_size() for t in (self._keys, self._values))
+        """Allocated persistent payload (int8 rows plus fp32 scales when quantized)."""
+        arrays = [self._keys, self._values]
+        if self.quantized:
+            arrays += [self._key_scales, self._value_scales]
+        return sum(t.numel() * t.element_size() for t in arrays)
 
     def __len__(self):
         return self.length

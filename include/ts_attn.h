@@ -34,7 +34,10 @@ extern "C" {
 
 /* Element types.  Half types compute in fp32 with fp32 softmax statistics,
  * as the reference does (nn/attention.py:63); fp64 computes in fp64. */
-typedef enum ts_dtype { TS_F32 = 0, TS_F16 = 1, TS_BF16 = 2, TS_F64 = 3 } ts_dtype;
+typedef enum ts_dtype { TS_F32 = 0, TS_F16 = 1, TS_BF16 = 2, TS_F64 = 3, TS_I8 = 4 } ts_dtype;
+/* TS_I8 is a storage type only: the int8 KV cache of nn/cache.py:47-52
+ * (ts_kv_append_int8, ts_kv_dequant_int8, ts_kv_reorder and the K/V views of
+ * ts_attn_decode_int8).  No attention entry point computes in it. */
 
 /* Optional attention mask of nn/attention.py:64-76, 105-107:
  * BOOL  -- uint8 0/1, True (1) = allowed, False -> score -inf;
@@ -189,6 +192,39 @@ TS_ATTN_API int ts_kv_reorder(ts_view4 src, ts_view4 dst, int32_t dtype, int32_t
  * share the array and race.  Returns TS_ERR_WORKSPACE, launching nothing, when
  * the problem needs more scratch than that.  Allocates nothing. */
 TS_ATTN_API int ts_attn_decode_noalloc(const ts_attn_params* params, void* stream);
+
+/* Quantising KVCache.append of nn/cache.py:54-86 with quantized=True.
+ * key_cache / value_cache are int8 views; params->cache_dtype is the cache's
+ * compute dtype (rows are rounded to it first, :68).  Per row:
+ * scale = max(max|x| / 127, 1e-8) in fp32, q = round_half_even(x / scale)
+ * (:70-75).  key_scales / value_scales are contiguous fp32 [batch, heads,
+ * capacity] (the reference's [B, H, capacity, 1]). */
+TS_ATTN_API int ts_kv_append_int8(const ts_kv_append_params* params, float* key_scales, float* value_scales,
+                                  void* stream);
+
+/* KVCache.get of a quantized cache (nn/cache.py:88-99):
+ * dst[b, h, t, c] = dtype(float(src[b, h, t, c]) * scales[b, h, t]) for
+ * t < length; scales contiguous [batch, heads, scale_capacity]. */
+TS_ATTN_API int ts_kv_dequant_int8(ts_view4 src, const float* scales, int64_t scale_capacity, ts_view4 dst,
+                                   int32_t dtype, int32_t batch, int32_t heads, int32_t length, int32_t channels,
+                                   void* stream);
+
+/* Workspace bytes ts_attn_decode_int8 needs (0 when one split suffices). */
+TS_ATTN_API size_t ts_attn_decode_int8_workspace_size(const ts_attn_params* params);
+
+/* Decode straight from an int8 KV cache (replaces nn/cache.py:91-99 followed
+ * by nn/attention.py:132-145): params->k / params->v are int8 views (element
+ * strides = bytes), params->dtype is the dtype of q and o, scales as in
+ * ts_kv_append_int8 with `scale_capacity` keys per (row, head).  Scores are
+ * k_scale * (q . k8) and probabilities meet v_scale * v8, in fp32; the
+ * dequantised rows are never written.  Same masking rules as ts_attn_decode
+ * (causal, causal_offset, kv_lens; no explicit mask).  TS_ERR_UNSUPPORTED when
+ * the shape is outside the kernel (head_dim = value_dim in {64, 128, 256},
+ * 16-byte aligned rows): dequantise with ts_kv_dequant_int8 and call
+ * ts_attn_fwd instead. */
+TS_ATTN_API int ts_attn_decode_int8(const ts_attn_params* params, const float* key_scales,
+                                    const float* value_scales, int64_t scale_capacity, void* workspace,
+                                    size_t workspace_bytes, void* stream);
 
 /* Reads and clears the device fault word written by kernels whose bounded
  * waits gave up.  Synchronises `stream`.  Returns TS_OK or
