@@ -173,6 +173,56 @@ int ts_kv_reorder(ts_view4 src, ts_view4 dst, int32_t dtype, int32_t batch, int3
   return from_cuda(tsa::kv_reorder(src, dst, dtype, batch, heads, length, channels, index, as_stream(stream)));
 }
 
+}  // extern "C"
+
+namespace {
+bool make_dropout(const ts_dropout* d, tsa::DropoutArgs& out) {
+  if (!d || !(d->p >= 0.0) || !(d->p < 1.0)) return false;
+  out.p = (float)d->p;
+  out.inv_keep_f = 1.0f / (float)(1.0 - d->p);
+  out.inv_keep_d = 1.0 / (1.0 - d->p);
+  out.seed = d->seed;
+  out.offset = d->offset;
+  return true;
+}
+}  // namespace
+
+extern "C" {
+
+int ts_attn_fwd_dropout(const ts_attn_params* p, const ts_dropout* d, void* stream) {
+  const int st = check_params(p);
+  if (st != TS_OK) return st;
+  tsa::DropoutArgs args;
+  if (!make_dropout(d, args)) return TS_ERR_INVALID_ARGUMENT;
+  return from_cuda(tsa::simt_forward(*p, as_stream(stream), d->p > 0.0 ? &args : nullptr));
+}
+
+size_t ts_attn_bwd_dropout_workspace_size(const ts_attn_bwd_params* bp) {
+  if (!bp || check_params(&bp->fwd) != TS_OK) return 0;
+  return tsa::simt_backward_workspace(*bp);
+}
+
+int ts_attn_bwd_dropout(const ts_attn_bwd_params* bp, const ts_dropout* d, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  if (!bp) return TS_ERR_INVALID_ARGUMENT;
+  const int st = check_params(&bp->fwd);
+  if (st != TS_OK) return st;
+  if (!bp->fwd.lse || !bp->dout.data || !bp->dq.data || !bp->dk.data || !bp->dv.data)
+    return TS_ERR_INVALID_ARGUMENT;
+  tsa::DropoutArgs args;
+  if (!make_dropout(d, args)) return TS_ERR_INVALID_ARGUMENT;
+  if (!workspace || workspace_bytes < tsa::simt_backward_workspace(*bp)) return TS_ERR_WORKSPACE;
+  return from_cuda(tsa::simt_backward(*bp, workspace, as_stream(stream), d->p > 0.0 ? &args : nullptr));
+}
+
+int ts_attn_dropout_mask(const ts_dropout* d, int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
+                         uint8_t* mask, void* stream) {
+  tsa::DropoutArgs args;
+  if (!make_dropout(d, args) || !mask || batch <= 0 || heads <= 0 || q_len <= 0 || kv_len <= 0)
+    return TS_ERR_INVALID_ARGUMENT;
+  return from_cuda(tsa::dropout_mask(args, batch, heads, q_len, kv_len, mask, as_stream(stream)));
+}
+
 int ts_kv_append_int8(const ts_kv_append_params* p, float* key_scales, float* value_scales, void* stream) {
   if (!p) return TS_ERR_INVALID_ARGUMENT;
   if (!dtype_ok(p->src_dtype) || !dtype_ok(p->cache_dtype)) return TS_ERR_UNSUPPORTED;

@@ -9,12 +9,16 @@
 //   forward     :175-198  online softmax, output a/l, LSE = m + log l (-inf if l = 0)
 //   backward    :220-244  p = exp(s - LSE), ds = p (dO.v - rowsum(dO*O)) * scale
 //   GQA reduce  :245-247  dK/dV summed over the query heads of a KV group
+//   dropout     :140-144, 212-216 (kDrop instantiations): P.V uses p * keep / (1 - p),
+//               dP is multiplied by the same factor; the mask is regenerated from a
+//               counter-based generator (dropout.cuh) in every kernel.
 //
 // Thread layout: a group of G consecutive threads owns one row (a query row in
 // the forward / dQ kernels, a key row in the dK/dV kernel).  Thread g of the
 // group holds channels g, g+G, g+2G, ... so the G threads of a group read
 // consecutive shared-memory words (no bank conflicts) and a row's dot product
 // is a G-lane butterfly.
+#include "dropout.cuh"
 #include "simt.cuh"
 
 namespace tsa {
@@ -84,8 +88,8 @@ __device__ __forceinline__ void stage_rows(A* dst, const ts_view4& src, int b, i
 // ---------------------------------------------------------------------------
 // Forward: one query row per G-thread group.
 // ---------------------------------------------------------------------------
-template <typename T, int G>
-__global__ void __launch_bounds__(kSimtThreads) simt_fwd_kernel(ts_attn_params p) {
+template <typename T, int G, bool kDrop>
+__global__ void __launch_bounds__(kSimtThreads) simt_fwd_kernel(ts_attn_params p, DropoutArgs drop) {
   using A = typename Elem<T>::acc;
   constexpr int DPT = SimtCfg<A>::DPT;
   constexpr int R = kSimtThreads / G;
@@ -144,14 +148,23 @@ __global__ void __launch_bounds__(kSimtThreads) simt_fwd_kernel(ts_attn_params p
     l *= corr;
 #pragma unroll
     for (int k = 0; k < DPT; ++k) o[k] *= corr;
+    uint32_t keep = 0xffffffffu;
+    if constexpr (kDrop) {
+      keep = 0;
+      const uint32_t bh = (uint32_t)(b * p.q_heads + h);
+#pragma unroll
+      for (int j4 = 0; j4 < kSimtKeys / 4; ++j4)
+        keep |= dropout_keep4(drop, bh, (uint32_t)i, (uint32_t)(k0 / 4 + j4)) << (4 * j4);
+    }
 #pragma unroll
     for (int jj = 0; jj < kSimtKeys; ++jj) {
       const A pj = acc_exp(s[jj] - safe);
       l += pj;
+      const A pv = kDrop ? ((keep >> jj) & 1u ? pj * dropout_scale<A>(drop) : A(0)) : pj;
 #pragma unroll
       for (int k = 0; k < DPT; ++k) {
         const int d = g + G * k;
-        if (d < Dv) o[k] += pj * vs[jj * Dv + d];
+        if (d < Dv) o[k] += pv * vs[jj * Dv + d];
       }
     }
     m = m_new;
@@ -192,9 +205,9 @@ __global__ void simt_bwd_delta_kernel(ts_attn_bwd_params bp, typename Elem<T>::a
 // ---------------------------------------------------------------------------
 // dQ: one query row per group; loops over the row's visible keys.
 // ---------------------------------------------------------------------------
-template <typename T, int G>
+template <typename T, int G, bool kDrop>
 __global__ void __launch_bounds__(kSimtThreads)
-    simt_bwd_dq_kernel(ts_attn_bwd_params bp, const typename Elem<T>::acc* delta) {
+    simt_bwd_dq_kernel(ts_attn_bwd_params bp, const typename Elem<T>::acc* delta, DropoutArgs drop) {
   using A = typename Elem<T>::acc;
   constexpr int DPT = SimtCfg<A>::DPT;
   constexpr int R = kSimtThreads / G;
@@ -239,6 +252,14 @@ __global__ void __launch_bounds__(kSimtThreads)
     stage_rows<T, A>(ks, p.k, b, hk, k0, kSimtKeys, kv_end, D);
     stage_rows<T, A>(vs, p.v, b, hk, k0, kSimtKeys, kv_end, Dv);
     __syncthreads();
+    uint32_t keep = 0xffffffffu;
+    if constexpr (kDrop) {
+      keep = 0;
+      const uint32_t bh = (uint32_t)(b * p.q_heads + h);
+#pragma unroll
+      for (int j4 = 0; j4 < kSimtKeys / 4; ++j4)
+        keep |= dropout_keep4(drop, bh, (uint32_t)i, (uint32_t)(k0 / 4 + j4)) << (4 * j4);
+    }
 #pragma unroll 4
     for (int jj = 0; jj < kSimtKeys; ++jj) {
       A sp = A(0), dp = A(0);
@@ -254,6 +275,7 @@ __global__ void __launch_bounds__(kSimtThreads)
       bool ok = live && j < kv_end && (!p.is_causal || (int64_t)i + offset >= j);
       if (ok) ok = mask_apply<A>(p, b, h, i, j, sp);
       const A pr = ok ? acc_exp(sp - lse) : A(0);
+      if constexpr (kDrop) dp = (keep >> jj) & 1u ? dp * dropout_scale<A>(drop) : A(0);
       const A ds = pr * (dp - dlt) * scale;
 #pragma unroll
       for (int k = 0; k < DPT; ++k) {
@@ -274,9 +296,9 @@ __global__ void __launch_bounds__(kSimtThreads)
 // dK / dV: one key row per group; loops over every query head of the KV
 // group and the query rows that see the key (GQA reduction in registers).
 // ---------------------------------------------------------------------------
-template <typename T, int G>
+template <typename T, int G, bool kDrop>
 __global__ void __launch_bounds__(kSimtThreads)
-    simt_bwd_dkdv_kernel(ts_attn_bwd_params bp, const typename Elem<T>::acc* delta) {
+    simt_bwd_dkdv_kernel(ts_attn_bwd_params bp, const typename Elem<T>::acc* delta, DropoutArgs drop) {
   using A = typename Elem<T>::acc;
   constexpr int DPT = SimtCfg<A>::DPT;
   constexpr int R = kSimtThreads / G;
@@ -354,11 +376,18 @@ __global__ void __launch_bounds__(kSimtThreads)
         bool ok = key_ok && lv[ii] && (!p.is_causal || (int64_t)i + offset >= j);
         if (ok) ok = mask_apply<A>(p, b, h, i, j, sp);
         const A pr = ok ? acc_exp(sp - ls[ii]) : A(0);
+        A pv = pr;
+        if constexpr (kDrop) {
+          const A f = dropout_keep(drop, (uint32_t)(b * p.q_heads + h), (uint32_t)i, (uint32_t)j)
+                          ? dropout_scale<A>(drop) : A(0);
+          pv = pr * f;
+          dp = dp * f;
+        }
         const A dsv = pr * (dp - ds_[ii]) * scale;
 #pragma unroll
         for (int k = 0; k < DPT; ++k) {
           const int d = g + G * k;
-          if (d < Dv) dv[k] += pr * gs[ii * Dv + d];
+          if (d < Dv) dv[k] += pv * gs[ii * Dv + d];
           if (d < D) dk[k] += dsv * qs[ii * D + d];
         }
       }
@@ -384,21 +413,22 @@ template <typename A> static int simt_group(int dmax) {
 }
 
 template <typename T, int G>
-static cudaError_t launch_fwd_g(const ts_attn_params& p, cudaStream_t st) {
+static cudaError_t launch_fwd_g(const ts_attn_params& p, const DropoutArgs* drop, cudaStream_t st) {
   using A = typename Elem<T>::acc;
   constexpr int R = kSimtThreads / G;
   const size_t smem = sizeof(A) * kSimtKeys * (p.head_dim + p.value_dim);
-  auto kern = simt_fwd_kernel<T, G>;
+  auto kern = drop ? simt_fwd_kernel<T, G, true> : simt_fwd_kernel<T, G, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid(ceil_div(p.q_len, R), p.q_heads, p.batch);
-  kern<<<grid, kSimtThreads, smem, st>>>(p);
+  kern<<<grid, kSimtThreads, smem, st>>>(p, drop ? *drop : DropoutArgs{});
   return cudaGetLastError();
 }
 
 template <typename T, int G>
 static cudaError_t launch_bwd_g(const ts_attn_bwd_params& bp, typename Elem<T>::acc* delta,
-                                cudaStream_t st) {
+                                const DropoutArgs* drop, cudaStream_t st) {
+  const DropoutArgs d = drop ? *drop : DropoutArgs{};
   using A = typename Elem<T>::acc;
   constexpr int R = kSimtThreads / G;
   const ts_attn_params& p = bp.fwd;
@@ -408,45 +438,45 @@ static cudaError_t launch_bwd_g(const ts_attn_bwd_params& bp, typename Elem<T>::
   if (e != cudaSuccess) return e;
 
   const size_t smem_dq = sizeof(A) * kSimtKeys * (p.head_dim + p.value_dim);
-  auto kdq = simt_bwd_dq_kernel<T, G>;
+  auto kdq = drop ? simt_bwd_dq_kernel<T, G, true> : simt_bwd_dq_kernel<T, G, false>;
   e = cudaFuncSetAttribute(kdq, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_dq);
   if (e != cudaSuccess) return e;
-  kdq<<<dim3(ceil_div(p.q_len, R), p.q_heads, p.batch), kSimtThreads, smem_dq, st>>>(bp, delta);
+  kdq<<<dim3(ceil_div(p.q_len, R), p.q_heads, p.batch), kSimtThreads, smem_dq, st>>>(bp, delta, d);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
   const size_t smem_kv = sizeof(A) * (kSimtQRows * (p.head_dim + p.value_dim) + 2 * kSimtQRows) +
                          kSimtQRows;
-  auto kkv = simt_bwd_dkdv_kernel<T, G>;
+  auto kkv = drop ? simt_bwd_dkdv_kernel<T, G, true> : simt_bwd_dkdv_kernel<T, G, false>;
   e = cudaFuncSetAttribute(kkv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_kv);
   if (e != cudaSuccess) return e;
-  kkv<<<dim3(ceil_div(p.kv_len, R), p.kv_heads, p.batch), kSimtThreads, smem_kv, st>>>(bp, delta);
+  kkv<<<dim3(ceil_div(p.kv_len, R), p.kv_heads, p.batch), kSimtThreads, smem_kv, st>>>(bp, delta, d);
   return cudaGetLastError();
 }
 
 template <typename T>
-static cudaError_t simt_fwd_t(const ts_attn_params& p, cudaStream_t st) {
+static cudaError_t simt_fwd_t(const ts_attn_params& p, const DropoutArgs* drop, cudaStream_t st) {
   using A = typename Elem<T>::acc;
   switch (simt_group<A>(max(p.head_dim, p.value_dim))) {
-    case 1: return launch_fwd_g<T, 1>(p, st);
-    case 2: return launch_fwd_g<T, 2>(p, st);
-    case 4: return launch_fwd_g<T, 4>(p, st);
-    case 8: return launch_fwd_g<T, 8>(p, st);
-    case 16: return launch_fwd_g<T, 16>(p, st);
+    case 1: return launch_fwd_g<T, 1>(p, drop, st);
+    case 2: return launch_fwd_g<T, 2>(p, drop, st);
+    case 4: return launch_fwd_g<T, 4>(p, drop, st);
+    case 8: return launch_fwd_g<T, 8>(p, drop, st);
+    case 16: return launch_fwd_g<T, 16>(p, drop, st);
     default: return cudaErrorInvalidValue;
   }
 }
 
 template <typename T>
-static cudaError_t simt_bwd_t(const ts_attn_bwd_params& bp, void* ws, cudaStream_t st) {
+static cudaError_t simt_bwd_t(const ts_attn_bwd_params& bp, void* ws, const DropoutArgs* drop, cudaStream_t st) {
   using A = typename Elem<T>::acc;
   A* delta = reinterpret_cast<A*>(ws);
   switch (simt_group<A>(max(bp.fwd.head_dim, bp.fwd.value_dim))) {
-    case 1: return launch_bwd_g<T, 1>(bp, delta, st);
-    case 2: return launch_bwd_g<T, 2>(bp, delta, st);
-    case 4: return launch_bwd_g<T, 4>(bp, delta, st);
-    case 8: return launch_bwd_g<T, 8>(bp, delta, st);
-    case 16: return launch_bwd_g<T, 16>(bp, delta, st);
+    case 1: return launch_bwd_g<T, 1>(bp, delta, drop, st);
+    case 2: return launch_bwd_g<T, 2>(bp, delta, drop, st);
+    case 4: return launch_bwd_g<T, 4>(bp, delta, drop, st);
+    case 8: return launch_bwd_g<T, 8>(bp, delta, drop, st);
+    case 16: return launch_bwd_g<T, 16>(bp, delta, drop, st);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -463,12 +493,12 @@ cudaError_t simt_delta_f32(const ts_attn_bwd_params& bp, float* delta, cudaStrea
   return cudaGetLastError();
 }
 
-cudaError_t simt_forward(const ts_attn_params& p, cudaStream_t st) {
+cudaError_t simt_forward(const ts_attn_params& p, cudaStream_t st, const DropoutArgs* drop) {
   switch (p.dtype) {
-    case TS_F32: return simt_fwd_t<float>(p, st);
-    case TS_F64: return simt_fwd_t<double>(p, st);
-    case TS_F16: return simt_fwd_t<__half>(p, st);
-    case TS_BF16: return simt_fwd_t<__nv_bfloat16>(p, st);
+    case TS_F32: return simt_fwd_t<float>(p, drop, st);
+    case TS_F64: return simt_fwd_t<double>(p, drop, st);
+    case TS_F16: return simt_fwd_t<__half>(p, drop, st);
+    case TS_BF16: return simt_fwd_t<__nv_bfloat16>(p, drop, st);
   }
   return cudaErrorInvalidValue;
 }
@@ -478,14 +508,32 @@ size_t simt_backward_workspace(const ts_attn_bwd_params& bp) {
   return acc * (size_t)bp.fwd.batch * bp.fwd.q_heads * bp.fwd.q_len;
 }
 
-cudaError_t simt_backward(const ts_attn_bwd_params& bp, void* ws, cudaStream_t st) {
+cudaError_t simt_backward(const ts_attn_bwd_params& bp, void* ws, cudaStream_t st, const DropoutArgs* drop) {
   switch (bp.fwd.dtype) {
-    case TS_F32: return simt_bwd_t<float>(bp, ws, st);
-    case TS_F64: return simt_bwd_t<double>(bp, ws, st);
-    case TS_F16: return simt_bwd_t<__half>(bp, ws, st);
-    case TS_BF16: return simt_bwd_t<__nv_bfloat16>(bp, ws, st);
+    case TS_F32: return simt_bwd_t<float>(bp, ws, drop, st);
+    case TS_F64: return simt_bwd_t<double>(bp, ws, drop, st);
+    case TS_F16: return simt_bwd_t<__half>(bp, ws, drop, st);
+    case TS_BF16: return simt_bwd_t<__nv_bfloat16>(bp, ws, drop, st);
   }
   return cudaErrorInvalidValue;
+}
+
+// One CTA per (query row, head, batch row); threads over keys in groups of 4.
+__global__ void dropout_mask_kernel(DropoutArgs d, int heads, int q_len, int kv_len, uint8_t* mask) {
+  const int i = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const uint32_t bh = (uint32_t)(b * heads + h);
+  uint8_t* row = mask + (((int64_t)b * heads + h) * q_len + i) * kv_len;
+  for (int j4 = threadIdx.x; j4 * 4 < kv_len; j4 += blockDim.x) {
+    const uint32_t bits = dropout_keep4(d, bh, (uint32_t)i, (uint32_t)j4);
+    for (int k = 0; k < 4 && j4 * 4 + k < kv_len; ++k) row[j4 * 4 + k] = (bits >> k) & 1u;
+  }
+}
+
+cudaError_t dropout_mask(const DropoutArgs& d, int batch, int heads, int q_len, int kv_len, uint8_t* mask,
+                         cudaStream_t st) {
+  if (q_len > 65535 * 32 || heads > 65535 || batch > 65535) return cudaErrorInvalidValue;
+  dropout_mask_kernel<<<dim3(q_len, heads, batch), 128, 0, st>>>(d, heads, q_len, kv_len, mask);
+  return cudaGetLastError();
 }
 
 }  // namespace tsa

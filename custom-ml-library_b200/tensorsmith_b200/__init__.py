@@ -8,6 +8,7 @@ node.  There is no CPU fallback.
 """
 
 from . import engine, nn  # noqa: F401
+from .engine import seed  # noqa: F401
 from .tensor import Tensor, enable_grad, is_grad_enabled, no_grad, tensor  # noqa: F401
 
 __version__ = "0.1.0"

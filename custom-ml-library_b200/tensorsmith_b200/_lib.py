@@ -70,6 +70,10 @@ class AttnBwdParams(ctypes.Structure):
     _fields_ = [("fwd", AttnParams), ("dout", View4), ("dq", View4), ("dk", View4), ("dv", View4)]
 
 
+class Dropout(ctypes.Structure):
+    _fields_ = [("p", ctypes.c_double), ("seed", ctypes.c_uint64), ("offset", ctypes.c_uint64)]
+
+
 class KvAppendParams(ctypes.Structure):
     _fields_ = [
         ("key", View4),
@@ -121,6 +125,17 @@ SIGNATURES = {
         ctypes.c_int,
         [View4, View4, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
          ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p],
+    ),
+    "ts_attn_fwd_dropout": (ctypes.c_int, [ctypes.POINTER(AttnParams), ctypes.POINTER(Dropout), ctypes.c_void_p]),
+    "ts_attn_bwd_dropout_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(AttnBwdParams)]),
+    "ts_attn_bwd_dropout": (
+        ctypes.c_int,
+        [ctypes.POINTER(AttnBwdParams), ctypes.POINTER(Dropout), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p],
+    ),
+    "ts_attn_dropout_mask": (
+        ctypes.c_int,
+        [ctypes.POINTER(Dropout), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
+         ctypes.c_void_p],
     ),
     "ts_kv_append_int8": (
         ctypes.c_int, [ctypes.POINTER(KvAppendParams), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]

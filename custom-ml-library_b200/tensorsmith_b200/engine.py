@@ -128,11 +128,20 @@ def fwd_path(q, k, v, *, decode=False, is_causal=False, scale=None, causal_offse
     return _lib.PATH_NAMES[code]
 
 
+def _dropout_struct(dropout) -> _lib.Dropout:
+    p, seed, offset = dropout
+    if not 0.0 <= float(p) < 1.0:
+        raise ValueError("dropout probability must be in [0, 1)")
+    return _lib.Dropout(float(p), int(seed) & (2**64 - 1), int(offset) & (2**64 - 1))
+
+
 def forward(q, k, v, *, is_causal=False, scale=None, causal_offset=0, kv_lens=None, mask=None,
-            need_lse=True, out=None, lse=None):
+            need_lse=True, out=None, lse=None, dropout=None):
     """Attention forward: returns ``(out [B,Hq,Tq,Dv], lse [B,Hq,Tq] or None)``.
 
-    ``lse`` is fp32 (fp64 for fp64 inputs), natural-log units, -inf on fully masked rows."""
+    ``lse`` is fp32 (fp64 for fp64 inputs), natural-log units, -inf on fully masked rows.
+    ``dropout = (p, seed, offset)`` applies attention dropout (ts_attn_fwd_dropout); pass
+    the same tuple to ``backward``."""
     _check_inputs(q, k, v)
     b, hq, tq, _ = q.shape
     if out is None:
@@ -141,7 +150,12 @@ def forward(q, k, v, *, is_causal=False, scale=None, causal_offset=0, kv_lens=No
         lse = torch.empty((b, hq, tq), dtype=lse_dtype(q.dtype), device=q.device)
     p, keep = make_params(q, k, v, out, lse if need_lse else None, is_causal=is_causal, scale=scale,
                           causal_offset=causal_offset, kv_lens=kv_lens, mask=mask)
-    _lib.check(_lib.lib().ts_attn_fwd(ctypes.byref(p), _stream_handle(q.device)), "ts_attn_fwd")
+    if dropout is not None:
+        d = _dropout_struct(dropout)
+        _lib.check(_lib.lib().ts_attn_fwd_dropout(ctypes.byref(p), ctypes.byref(d), _stream_handle(q.device)),
+                   "ts_attn_fwd_dropout")
+    else:
+        _lib.check(_lib.lib().ts_attn_fwd(ctypes.byref(p), _stream_handle(q.device)), "ts_attn_fwd")
     del keep
     return out, (lse if need_lse else None)
 
@@ -220,8 +234,9 @@ def bwd_path(q, k, v, out, lse, dout, **kw) -> str:
 
 
 def backward(q, k, v, out, lse, dout, *, is_causal=False, scale=None, causal_offset=0, kv_lens=None,
-             mask=None, dq=None, dk=None, dv=None):
-    """dQ, dK, dV of attention from the forward output and its LSE."""
+             mask=None, dq=None, dk=None, dv=None, dropout=None):
+    """dQ, dK, dV of attention from the forward output and its LSE (``dropout`` as given
+    to the forward)."""
     _check_inputs(q, k, v)
     _require_cuda(out, lse, dout)
     dq = torch.empty_like(q) if dq is None else dq
@@ -232,12 +247,55 @@ def backward(q, k, v, out, lse, dout, *, is_causal=False, scale=None, causal_off
     bp, keep = _bwd_params(q, k, v, out, lse, dout, dq, dk, dv, is_causal=is_causal, scale=scale,
                            causal_offset=causal_offset, kv_lens=kv_lens, mask=mask)
     handle = _lib.lib()
+    if dropout is not None:
+        d = _dropout_struct(dropout)
+        need = int(handle.ts_attn_bwd_dropout_workspace_size(ctypes.byref(bp)))
+        ws = torch.empty(max(need, 16), dtype=torch.uint8, device=q.device)
+        _lib.check(handle.ts_attn_bwd_dropout(ctypes.byref(bp), ctypes.byref(d), ws.data_ptr(), ws.numel(),
+                                              _stream_handle(q.device)), "ts_attn_bwd_dropout")
+        del keep
+        return dq, dk, dv
     need = int(handle.ts_attn_bwd_workspace_size(ctypes.byref(bp)))
     ws = torch.empty(max(need, 16), dtype=torch.uint8, device=q.device)
     _lib.check(handle.ts_attn_bwd(ctypes.byref(bp), ws.data_ptr(), ws.numel(), _stream_handle(q.device)),
                "ts_attn_bwd")
     del keep
     return dq, dk, dv
+
+
+def dropout_mask(batch, heads, q_len, kv_len, dropout, device) -> torch.Tensor:
+    """The uint8 keep mask [B, Hq, Tq, Tk] that ``dropout = (p, seed, offset)`` applies."""
+    d = _dropout_struct(dropout)
+    mask = torch.empty((batch, heads, q_len, kv_len), dtype=torch.uint8, device=device)
+    _lib.check(_lib.lib().ts_attn_dropout_mask(ctypes.byref(d), batch, heads, q_len, kv_len, mask.data_ptr(),
+                                               _stream_handle(mask.device)), "ts_attn_dropout_mask")
+    return mask
+
+
+class _DropoutGenerator:
+    """(seed, offset) source for attention dropout: ``seed()`` resets it, every draw
+    takes the next offset (the counter that keeps calls' masks independent)."""
+
+    def __init__(self):
+        self.seed_value = int(torch.initial_seed()) & (2**64 - 1)
+        self.offset = 0
+
+    def seed(self, value: int) -> None:
+        self.seed_value = int(value) & (2**64 - 1)
+        self.offset = 0
+
+    def draw(self, p: float) -> tuple:
+        args = (float(p), self.seed_value, self.offset)
+        self.offset += 1
+        return args
+
+
+DROPOUT_GENERATOR = _DropoutGenerator()
+
+
+def seed(value: int) -> None:
+    """Seed the attention-dropout generator (tensorsmith's ``ts.seed``, device.py:226-232)."""
+    DROPOUT_GENERATOR.seed(value)
 
 
 def kv_append(key, value, key_cache, value_cache, *, position=0, positions=None, positions_out=None):

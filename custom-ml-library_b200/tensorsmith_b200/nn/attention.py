@@ -81,14 +81,27 @@ def scaled_dot_product_attention(
             mask.expand(b, h, qlen, key.shape[2])
         except RuntimeError as error:
             raise ValueError("attention mask is not broadcastable to [B,H,Q,K]") from error
-    selected = "native" if backend == "auto" else backend
-    if dropout_p:
-        raise ValueError("attention dropout is not supported by the B200 engine kernels")
+    # Backend names select nothing on CUDA (every one is exact attention on the engine),
+    # but dropout keeps the reference's rule: dense only (nn/attention.py:76-83).
+    selected = ("dense" if dropout_p else "native") if backend == "auto" else backend
+    if selected in {"native", "streaming"} and dropout_p:
+        raise ValueError("attention dropout currently requires the dense backend")
 
     recording = is_grad_enabled() and any(t.requires_grad for t in (query, key, value))
     q, k, v = query._data, key._data, value._data
     kwargs = dict(is_causal=is_causal, scale=multiplier, causal_offset=causal_offset,
                   kv_lens=kv_lens, mask=mask)
+    if dropout_p:
+        # One draw of the generator per call; the backward reuses it (nn/attention.py:140-144, 212-216).
+        kwargs["dropout"] = engine.DROPOUT_GENERATOR.draw(dropout_p)
+        output, lse = engine.forward(q, k, v, need_lse=True, **kwargs)
+        if not recording:
+            return Tensor(output, device=query.device)
+
+        def backward_dropout(upstream):
+            return engine.backward(q, k, v, output, lse, upstream, **kwargs)
+
+        return Tensor._from_op(output, (query, key, value), backward_dropout, "sdpa_" + selected)
     if not recording:
         if repetitions * qlen <= engine.DECODE_MAX_ROWS and mask is None:
             output, _ = engine.decode(q, k, v, **kwargs)

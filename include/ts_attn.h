@@ -193,6 +193,35 @@ TS_ATTN_API int ts_kv_reorder(ts_view4 src, ts_view4 dst, int32_t dtype, int32_t
  * the problem needs more scratch than that.  Allocates nothing. */
 TS_ATTN_API int ts_attn_decode_noalloc(const ts_attn_params* params, void* stream);
 
+/* Attention dropout of nn/attention.py:140-144 (forward) and :212-216
+ * (backward): P.V uses p * keep / (1 - p) with keep = (u >= p), u uniform in
+ * [0, 1) per (batch, query head, query row, key); dP is multiplied by the same
+ * factor; LSE stays the softmax normaliser.  u comes from a counter-based
+ * generator (Philox4x32-10) keyed by (seed, offset), so a backward given the
+ * forward's (seed, offset) regenerates its mask without storing it. */
+typedef struct ts_dropout {
+  double p;        /* drop probability, 0 <= p < 1 */
+  uint64_t seed;   /* generator key */
+  uint64_t offset; /* call counter; a forward and its backward pass the same value */
+} ts_dropout;
+
+/* ts_attn_fwd with dropout (generic CUDA-core kernels, every dtype / shape /
+ * mask of ts_attn_fwd).  p = 0 is the plain forward on the same kernels. */
+TS_ATTN_API int ts_attn_fwd_dropout(const ts_attn_params* params, const ts_dropout* dropout, void* stream);
+
+/* Workspace bytes ts_attn_bwd_dropout needs. */
+TS_ATTN_API size_t ts_attn_bwd_dropout_workspace_size(const ts_attn_bwd_params* params);
+
+/* ts_attn_bwd for a forward made by ts_attn_fwd_dropout with the same dropout
+ * arguments. */
+TS_ATTN_API int ts_attn_bwd_dropout(const ts_attn_bwd_params* params, const ts_dropout* dropout, void* workspace,
+                                    size_t workspace_bytes, void* stream);
+
+/* The keep mask those calls use, as uint8 0/1 [batch, heads, q_len, kv_len]
+ * (contiguous; heads = query heads). */
+TS_ATTN_API int ts_attn_dropout_mask(const ts_dropout* dropout, int32_t batch, int32_t heads, int32_t q_len,
+                                     int32_t kv_len, uint8_t* mask, void* stream);
+
 /* Quantising KVCache.append of nn/cache.py:54-86 with quantized=True.
  * key_cache / value_cache are int8 views; params->cache_dtype is the cache's
  * compute dtype (rows are rounded to it first, :68).  Per row:

@@ -16,6 +16,7 @@ It restates, in NumPy, the algorithm of tensorsmith 0.3.0's attention path
     - dense forward                   :132-145
     - streaming online-softmax forward with saved LSE  :175-198
     - dense and blockwise VJP         :200-244
+    - attention dropout (dense only)  :140-144, 212-216
     - GQA gradient reduction          :245-247
 * ``rotary_embedding``               -- src/tensorsmith/nn/attention.py:255-296
 * ``KVCache``                        -- src/tensorsmith/nn/cache.py:12-142
@@ -108,8 +109,14 @@ def attention_forward(
     enable_gqa=False,
     algorithm="streaming",
     block_size=64,
+    dropout_keep=None,
+    dropout_p=0.0,
 ):
     """Forward of ``scaled_dot_product_attention`` (nn/attention.py:16-198).
+
+    ``dropout_keep`` (bool ``[B,Hq,Tq,Tk]``) with ``dropout_p`` applies the
+    reference's dense dropout (nn/attention.py:140-144): ``P * keep / (1 - p)``
+    before ``P V``; the LSE is unaffected.
 
     Returns ``(out, lse)`` in the compute dtype: out ``[B,Hq,Tq,Dv]`` and the
     natural-log normaliser ``lse`` ``[B,Hq,Tq]`` (``-inf`` for fully masked
@@ -126,9 +133,13 @@ def attention_forward(
         e = np.exp(s - m)
         total = np.sum(e, axis=-1, keepdims=True)
         p = e / np.where(total > 0, total, 1)
+        if dropout_keep is not None and dropout_p:
+            p = p * (np.asarray(dropout_keep).astype(cdt) / (1 - dropout_p))
         out = np.matmul(p, vc)
         lse = np.where(total > 0, m + np.log(np.where(total > 0, total, 1)), NEG_INF)
         return out.astype(cdt), lse[..., 0].astype(cdt)
+    if dropout_keep is not None and dropout_p:
+        raise ValueError("attention dropout currently requires the dense backend")
     if algorithm != "streaming":
         raise ValueError("algorithm must be dense or streaming")
     outs, lses = [], []
@@ -210,9 +221,11 @@ def attention_backward(
 
 
 def attention_backward_dense(
-    q, k, v, dout, mask=None, *, is_causal=False, scale=None, causal_offset=0, enable_gqa=False
+    q, k, v, dout, mask=None, *, is_causal=False, scale=None, causal_offset=0, enable_gqa=False,
+    dropout_keep=None, dropout_p=0.0,
 ):
-    """Dense VJP of nn/attention.py:200-219 (probabilities materialised)."""
+    """Dense VJP of nn/attention.py:200-219 (probabilities materialised), with the
+    forward's dropout mask when given (:212-216)."""
     qc, kc, vc, scale, mask, cdt = _prepare(q, k, v, mask, scale, enable_gqa)
     b, hq, tq, d = qc.shape
     tk = kc.shape[2]
@@ -222,8 +235,13 @@ def attention_backward_dense(
     e = np.exp(s - np.where(np.isfinite(m), m, 0))
     total = np.sum(e, axis=-1, keepdims=True)
     p = e / np.where(total > 0, total, 1)
-    dv = np.matmul(np.swapaxes(p, -1, -2), g)
+    drop = None
+    if dropout_keep is not None and dropout_p:
+        drop = np.asarray(dropout_keep).astype(cdt) / (1 - dropout_p)
+    dv = np.matmul(np.swapaxes(p if drop is None else p * drop, -1, -2), g)
     dp = np.matmul(g, np.swapaxes(vc, -1, -2))
+    if drop is not None:
+        dp = dp * drop
     ds = p * (dp - np.sum(dp * p, axis=-1, keepdims=True)) * scale
     dq = np.matmul(ds, kc)
     dk = np.matmul(np.swapaxes(ds, -1, -2), qc)

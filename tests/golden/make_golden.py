@@ -26,6 +26,12 @@ file:line of the behaviour each pins):
 * ``rope``        interleaved RoPE with offset and partial rotary_dim
   (nn/attention.py:255-296)
 * ``quant``       int8 KV cache round trip (nn/cache.py:70-98)
+* ``dropout``     dense attention with dropout_p=0.3 after ``ts.seed(8)``, fp32 and
+  fp64, with the keep mask the reference drew (nn/attention.py:140-144,
+  212-216; device.py:276-297 -- on the CPU backend the draw is
+  ``np.random.random(shape).astype(float32)`` right after the seed)
+
+``--only NAME`` regenerates one case and leaves the other files untouched.
 """
 
 from __future__ import annotations
@@ -200,10 +206,41 @@ def run(reference_src: str) -> dict:
     return meta
 
 
+def run_dropout(reference_src: str) -> None:
+    sys.path.insert(0, reference_src)
+    import tensorsmith as ts
+    from tensorsmith import nn
+
+    rng = np.random.default_rng(31)
+    shape_q, shape_k = (2, 3, 5, 8), (2, 3, 7, 8)
+    case = {}
+    for name in ("float32", "float64"):
+        arrays = [rng.normal(size=shape_q), rng.normal(size=shape_k), rng.normal(size=(2, 3, 7, 6))]
+        arrays = [a.astype(name) for a in arrays]
+        up = rng.normal(size=(2, 3, 5, 6)).astype(name)
+        tensors = [ts.tensor(a, requires_grad=True) for a in arrays]
+        ts.seed(8)
+        out = nn.scaled_dot_product_attention(*tensors, dropout_p=0.3, is_causal=True, causal_offset=2,
+                                              backend="dense")
+        out.backward(up)
+        np.random.seed(8)
+        draw = np.random.random((2, 3, 5, 7)).astype("float32")
+        case.update({f"{name}_q": arrays[0], f"{name}_k": arrays[1], f"{name}_v": arrays[2],
+                     f"{name}_dout": up, f"{name}_keep": draw >= 0.3, f"{name}_out": out.numpy(),
+                     f"{name}_dq": tensors[0].grad.numpy(), f"{name}_dk": tensors[1].grad.numpy(),
+                     f"{name}_dv": tensors[2].grad.numpy()})
+    np.savez_compressed(HERE / "dropout.npz", **case)
+
+
 def main():
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--reference", required=True, help="path to the tensorsmith src directory")
+    parser.add_argument("--only", default=None, help="regenerate one case (dropout)")
     args = parser.parse_args()
+    if args.only == "dropout":
+        run_dropout(args.reference)
+        return
+    run_dropout(args.reference)
     meta = run(args.reference)
     (HERE / "meta.json").write_text(json.dumps(meta, indent=2) + "\n")
     print(json.dumps(meta))

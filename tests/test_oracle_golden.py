@@ -141,3 +141,20 @@ def test_quantized_cache(golden):
 def test_causal_pairs_formula():
     assert oracle.causal_pairs(2, 4, 256, 256, 0) == 8 * 32896
     assert oracle.causal_pairs(1, 1, 3, 5, 2) == 3 + 4 + 5
+
+
+@pytest.mark.parametrize("name", ["float32", "float64"])
+def test_dropout_dense(golden, name):
+    """The reference's dense dropout forward + VJP with the mask it drew."""
+    case = golden("dropout")
+    q, k, v, g = (case[f"{name}_{x}"] for x in ("q", "k", "v", "dout"))
+    keep = case[f"{name}_keep"]
+    kw = dict(is_causal=True, causal_offset=2, dropout_keep=keep, dropout_p=0.3)
+    out, _ = oracle.attention_forward(q, k, v, algorithm="dense", **kw)
+    dq, dk, dv = oracle.attention_backward_dense(q, k, v, g, **kw)
+    tol = dict(rtol=1e-5, atol=1e-6) if name == "float32" else dict(rtol=1e-12, atol=1e-13)
+    for got, ref in ((out, "out"), (dq, "dq"), (dk, "dk"), (dv, "dv")):
+        np.testing.assert_allclose(got, case[f"{name}_{ref}"], err_msg=ref, **tol)
+    # Without the mask the outputs differ: the fixture really holds a dropped draw.
+    plain, _ = oracle.attention_forward(q, k, v, algorithm="dense", is_causal=True, causal_offset=2)
+    assert not np.allclose(plain, case[f"{name}_out"])
