@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import concurrent.futures
 import os
+import re
 import shutil
 import subprocess
 import sys
@@ -68,14 +69,33 @@ def stale() -> bool:
     return any(p.stat().st_mtime > built for p in deps)
 
 
+_INCLUDE_RE = re.compile(r'^\s*#\s*include\s*"([^"]+)"', re.M)
+
+
+def _local_deps(src: Path) -> set[Path]:
+    """The file plus every quoted include reachable from it in csrc/ and include/."""
+    seen: set[Path] = set()
+    stack = [src]
+    while stack:
+        path = stack.pop()
+        if path in seen or not path.exists():
+            continue
+        seen.add(path)
+        for name in _INCLUDE_RE.findall(path.read_text(errors="replace")):
+            for base in (path.parent, CSRC, INCLUDE):
+                if (base / name).exists():
+                    stack.append((base / name).resolve())
+                    break
+    return seen
+
+
 def _object_stale(src: Path) -> bool:
-    """An object is rebuilt when its source, any shared header, or the ABI header is newer."""
+    """An object is rebuilt when its source or a header it includes (transitively) is newer."""
     obj = BUILD / (src.stem + ".o")
     if not obj.exists():
         return True
-    deps = [src] + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
     built = obj.stat().st_mtime
-    return any(p.stat().st_mtime > built for p in deps)
+    return any(p.stat().st_mtime > built for p in _local_deps(src.resolve()))
 
 
 def build(force: bool = False, verbose_ptxas: bool = False, jobs: int | None = None) -> Path:
