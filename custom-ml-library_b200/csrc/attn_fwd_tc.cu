@@ -11,13 +11,20 @@
 //   warp 0   TMA producer: Q once, then K/V 128-key tiles into 2-stage rings
 //            (separate K and V rings so K(j+2) can land while P(j).V(j) runs)
 //   warp 1   MMA issuer (one thread): S = Q K^T into a double-buffered TMEM S,
-//            O += P V into TMEM O; completion signalled with tcgen05.commit
-//   warp 2   TMEM allocator (512 columns: S0 | S1 | O)
-//   warps 4-7 softmax warpgroup: thread r owns query row r (TMEM lane r):
-//            loads its S row (tcgen05.ld), exp2-domain online softmax with lazy
-//            rescaling (O is only rescaled when the running max grows by more
-//            than 2^8), writes P (bf16/f16) into a 128B-swizzled shared tile,
-//            then the epilogue O / l -> global and the LSE.
+//            then O_A += P_A V[0:64) and O_B += P_B V[64:128) into two TMEM
+//            accumulators; completion signalled with tcgen05.commit
+//   warp 2   TMEM allocator (512 columns: S0 | S1 | O_A | O_B)
+//   warps 4-7 and 8-11: two softmax warpgroups over the same 128 rows; group
+//            A owns keys [0, 64) of every tile, group B keys [64, 128).  Thread
+//            r of a group owns query row r (TMEM lane r) and runs an
+//            independent exp2-domain online softmax over its key half (its own
+//            running max and sum, lazy rescaling of its own O accumulator when
+//            the max grows by more than 2^8), writing P (bf16/f16) into its own
+//            64-key 128B-swizzled shared slab.  The halves never synchronise in
+//            the key loop; the epilogue merges them once:
+//            O = (O_A 2^(m_A-m) + O_B 2^(m_B-m)) / (l_A 2^(m_A-m) + l_B 2^(m_B-m)).
+//            Two warps per scheduler hide the TMEM-load and MUFU latencies that
+//            a single warpgroup of 128-key rows leaves exposed.
 // Shared-memory operands use the canonical 128-byte-swizzle layouts: Q, K and
 // P are K-major (8-row x 128-byte atoms, 1024 B apart); V is read MN-major
 // (64-channel blocks 16 KB apart, 8-key groups 1024 B apart).  No TMA load
@@ -46,12 +53,13 @@ template <int D> struct Cfg {
   static constexpr int kOffK = kOffQ + kTileBytes;
   static constexpr int kOffV = kOffK + kStages * kTileBytes;
   static constexpr int kOffP = kOffV + kStages * kTileBytes;
-  static constexpr int kOffBar = kOffP + 2 * kSlabBytes;
+  static constexpr int kOffRed = kOffP + 2 * kSlabBytes;  // epilogue exchange [half][row][m, l]
+  static constexpr int kOffBar = kOffRed + 2 * 128 * 2 * 4;
   static constexpr int kBarBytes = 256;
   static constexpr int kSmem = kOffBar + kBarBytes + 1024;  // +1024 alignment slack
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kColS = 0;     // two 128-column S buffers
-  static constexpr uint32_t kColO = 256;   // D columns
+  static constexpr uint32_t kColO = 256;   // O_A (D columns), then O_B (D columns)
 };
 
 struct Bars {
@@ -59,8 +67,9 @@ struct Bars {
   uint64_t k_full[3], k_empty[3];
   uint64_t v_full[3], v_empty[3];
   uint64_t s_full[2];
-  uint64_t p_full;
-  uint64_t o_done;
+  uint64_t p_full[2];  // per key half
+  uint64_t o_done[2];
+  uint64_t epi;        // both halves posted their (m, l)
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -75,7 +84,7 @@ struct TcFwdArgs {
 }  // namespace
 
 template <int D, bool kBF16>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(384, 1)
     tc_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, TcFwdArgs args) {
   using C = Cfg<D>;
@@ -118,8 +127,11 @@ __global__ void __launch_bounds__(256, 1)
     }
     ptx::mbar_init(&bars->s_full[0], 1);
     ptx::mbar_init(&bars->s_full[1], 1);
-    ptx::mbar_init(&bars->p_full, 4);
-    ptx::mbar_init(&bars->o_done, 1);
+    for (int hf = 0; hf < 2; ++hf) {
+      ptx::mbar_init(&bars->p_full[hf], 4);
+      ptx::mbar_init(&bars->o_done[hf], 1);
+    }
+    ptx::mbar_init(&bars->epi, 8);
     ptx::mbar_init(&bars->drain, 1);
     bars->abort = 0;
     ptx::fence_mbar_init();
@@ -170,24 +182,28 @@ __global__ void __launch_bounds__(256, 1)
     // ------------------------------ MMA issuer ----------------------------
     if (lane == 0 && n_tiles > 0 && !dead) {
       constexpr uint32_t idesc_qk = ptx::idesc_f16(kBF16, kBM, kBN, false, false);
-      constexpr uint32_t idesc_pv = ptx::idesc_f16(kBF16, kBM, D, false, true);
       const uint32_t sQa = ptx::smem_u32(sQ), sKa = ptx::smem_u32(sK), sVa = ptx::smem_u32(sV),
                      sPa = ptx::smem_u32(sP);
       bool ok = wait_bar(&bars->q_full, 0, args.fault, FAULT_FWD_Q);
       ptx::tc_fence_after();
+      constexpr uint32_t idesc_pv = ptx::idesc_f16(kBF16, kBM, D, false, true);
       auto issue_pv = [&](int jj) -> bool {
-        if (!wait_bar(&bars->p_full, jj & 1, args.fault, FAULT_FWD_P)) return false;
         const int s = jj % C::kStages;
         if (!wait_bar(&bars->v_full[s], (jj / C::kStages) & 1, args.fault, FAULT_FWD_KV)) return false;
-        ptx::tc_fence_after();
+        // Key half hf: P_hf (slab hf) times V keys [64 hf, 64 hf + 64) into O_hf.
+        for (int hf = 0; hf < 2; ++hf) {
+          if (!wait_bar(&bars->p_full[hf], jj & 1, args.fault, FAULT_FWD_P)) return false;
+          ptx::tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t a = ptx::sw128_desc(sPa + (kk >> 2) * kSlabBytes + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd =
-              ptx::sw128_desc(sVa + s * C::kTileBytes + kk * 16 * 128, kSlabBytes, 1024);
-          ptx::mma_f16_ss(tmem + C::kColO, a, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+          for (int kq = 0; kq < 4; ++kq) {
+            const int kk = hf * 4 + kq;
+            const uint64_t a = ptx::sw128_desc(sPa + hf * kSlabBytes + kq * 32, 16, 1024);
+            const uint64_t bd =
+                ptx::sw128_desc(sVa + s * C::kTileBytes + kk * 16 * 128, kSlabBytes, 1024);
+            ptx::mma_f16_ss(tmem + C::kColO + hf * D, a, bd, idesc_pv, (jj > 0 || kq > 0) ? 1u : 0u);
+          }
+          ptx::mma_commit(&bars->o_done[hf]);
         }
-        ptx::mma_commit(&bars->o_done);
         ptx::mma_commit(&bars->v_empty[s]);
         return true;
       };
@@ -217,11 +233,14 @@ __global__ void __launch_bounds__(256, 1)
       if (!ok) atomicExch(&bars->abort, 1);
     }
   } else if (warp >= 4) {
-    // ------------------------- softmax warpgroup ---------------------------
-    const int row = (warp - 4) * 32 + lane;
+    // ------------------------- softmax warpgroups --------------------------
+    const int half = (warp - 4) >> 2;           // 0: keys [0, 64) of a tile, 1: keys [64, 128)
+    const int row = (warp & 3) * 32 + lane;     // TMEM lane quarter = warp % 4
     const int qi = q0 + row;
     const uint32_t t_row = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const uint32_t col_o = C::kColO + (uint32_t)half * D;
     const float qk_scale = (float)p.scale * kLog2e;
+    constexpr int kHN = kBN / 2;  // keys per half
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = !dead;
     for (int j = 0; j < n_tiles && ok; ++j) {
@@ -231,31 +250,31 @@ __global__ void __launch_bounds__(256, 1)
         break;
       }
       ptx::tc_fence_after();
-      // All 128 raw scores of the row in registers (four loads, one wait).
-      uint32_t r[kBN];
+      // The 64 raw scores of this row's key half in registers (two loads, one wait).
+      uint32_t r[kHN];
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c)
-        ptx::tmem_ld32(t_row + C::kColS + (uint32_t)(j & 1) * kBN + 32 * c,
+      for (int c = 0; c < kHN / 32; ++c)
+        ptx::tmem_ld32(t_row + C::kColS + (uint32_t)(j & 1) * kBN + half * kHN + 32 * c,
                        *reinterpret_cast<uint32_t(*)[32]>(r + 32 * c));
       ptx::tmem_wait_ld();
-      const int k0 = j * kBN;
-      const bool need_mask = (k0 + kBN > kv_end) || (p.is_causal && (int64_t)k0 + kBN - 1 > (int64_t)q0 + offset);
+      const int k0 = j * kBN + half * kHN;
+      const bool need_mask = (k0 + kHN > kv_end) || (p.is_causal && (int64_t)k0 + kHN - 1 > (int64_t)q0 + offset);
       const int64_t lim = p.is_causal ? (int64_t)qi + offset : (int64_t)kv_end - 1;
-      // Row max of the (masked) raw scores, scaled once (scale > 0).  Tiles
+      // Row max of the (masked) raw scores, scaled once (scale > 0).  Halves
       // away from the diagonal and the sequence end take the unmasked branch
       // (warp-uniform).
       float mx = -INFINITY;
       if (!need_mask) {
         float m0 = -INFINITY, m1 = -INFINITY;  // two chains halve the dependent-max latency
 #pragma unroll
-        for (int c = 0; c < kBN; c += 4) {
+        for (int c = 0; c < kHN; c += 4) {
           m0 = ptx::max3(m0, __uint_as_float(r[c]), __uint_as_float(r[c + 1]));
           m1 = ptx::max3(m1, __uint_as_float(r[c + 2]), __uint_as_float(r[c + 3]));
         }
         mx = fmaxf(m0, m1);
       } else {
 #pragma unroll
-        for (int c = 0; c < kBN; ++c) {
+        for (int c = 0; c < kHN; ++c) {
           const int key = k0 + c;
           if (key < kv_end && (int64_t)key <= lim) mx = fmaxf(mx, __uint_as_float(r[c]));
         }
@@ -275,12 +294,12 @@ __global__ void __launch_bounds__(256, 1)
       // other element pair goes through MUFU ex2, the rest through the
       // FMA-pipe polynomial, and bf16 pairs are packed with integer rounding,
       // so the special function unit stays below the tensor core's time.
-      uint32_t pk[kBN / 2];
+      uint32_t pk[kHN / 2];
       uint64_t sum2[2] = {ptx::f2pack(0.f, 0.f), ptx::f2pack(0.f, 0.f)};
       if (!need_mask) {
         const uint64_t sc2 = ptx::f2pack(qk_scale, qk_scale), ng2 = ptx::f2pack(-safe, -safe);
 #pragma unroll
-        for (int c = 0; c < kBN; c += 2) {
+        for (int c = 0; c < kHN; c += 2) {
           const uint64_t x2 = ptx::fma2(ptx::f2pack(__uint_as_float(r[c]), __uint_as_float(r[c + 1])), sc2, ng2);
           uint64_t p2;
           if ((c & 2) == 0) {
@@ -297,7 +316,7 @@ __global__ void __launch_bounds__(256, 1)
         }
       } else {
 #pragma unroll
-        for (int c = 0; c < kBN; c += 2) {
+        for (int c = 0; c < kHN; c += 2) {
           const int key = k0 + c;
           float p0 = ptx::ex2(fmaf(__uint_as_float(r[c]), qk_scale, -safe));
           float p1 = ptx::ex2(fmaf(__uint_as_float(r[c + 1]), qk_scale, -safe));
@@ -313,8 +332,9 @@ __global__ void __launch_bounds__(256, 1)
         ptx::f2unpack(sum2[1], b0, b1);
         l_run += (a0 + a1) + (b0 + b1);
       }
-      // P buffer and O are free once P(j-1).V(j-1) has completed.
-      if (j >= 1 && !__all_sync(0xffffffffu, wait_bar(&bars->o_done, (j - 1) & 1, args.fault, FAULT_FWD_O))) {
+      // This half's P slab and O accumulator are free once P(j-1).V(j-1) of the half completed.
+      if (j >= 1 &&
+          !__all_sync(0xffffffffu, wait_bar(&bars->o_done[half], (j - 1) & 1, args.fault, FAULT_FWD_O))) {
         ok = false;
         break;
       }
@@ -323,24 +343,23 @@ __global__ void __launch_bounds__(256, 1)
       // so the whole warp takes it when any row needs it (factor 1 elsewhere).
       if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
         if (!rescale) factor = 1.f;
-        uint32_t r[32];
+        uint32_t o[32];
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
-          ptx::tmem_ld32(t_row + C::kColO + 32 * c, r);
+          ptx::tmem_ld32(t_row + col_o + 32 * c, o);
           ptx::tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * factor);
-          ptx::tmem_st32(t_row + C::kColO + 32 * c, r);
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
+          ptx::tmem_st32(t_row + col_o + 32 * c, o);
         }
         ptx::tmem_wait_st();
       }
-      // P row -> 128B-swizzled K-major tile: slab = 64 keys, 16-byte chunk c at (c ^ row%8).
-#pragma unroll
-      for (int sl = 0; sl < 2; ++sl) {
-        unsigned char* rowp = sP + sl * kSlabBytes + row * 128;
+      // P row -> this half's 128B-swizzled K-major slab: 16-byte chunk c at (c ^ row%8).
+      {
+        unsigned char* rowp = sP + half * kSlabBytes + row * 128;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          const int w = sl * 32 + c * 4;
+          const int w = c * 4;
           uint4 v = make_uint4(pk[w], pk[w + 1], pk[w + 2], pk[w + 3]);
           *reinterpret_cast<uint4*>(rowp + ((c ^ (row & 7)) << 4)) = v;
         }
@@ -348,46 +367,71 @@ __global__ void __launch_bounds__(256, 1)
       ptx::fence_proxy_async_smem();
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&bars->p_full);
+      if (lane == 0) ptx::mbar_arrive(&bars->p_full[half]);
     }
-    if (ok && n_tiles > 0)
-      ok = __all_sync(0xffffffffu, wait_bar(&bars->o_done, (n_tiles - 1) & 1, args.fault, FAULT_FWD_O));
+    // Epilogue: both O accumulators must be final (each thread reads both).
+    if (ok && n_tiles > 0) {
+      const uint32_t ph = (n_tiles - 1) & 1;
+      ok = __all_sync(0xffffffffu, wait_bar(&bars->o_done[0], ph, args.fault, FAULT_FWD_O) &&
+                                       wait_bar(&bars->o_done[1], ph, args.fault, FAULT_FWD_O));
+    }
     ptx::tc_fence_after();
-    // Epilogue: O / l -> global, LSE.
+    // Exchange (m, l) with the other half of the row, once.
+    float* red = reinterpret_cast<float*>(smem + C::kOffRed);
+    red[(half * 128 + row) * 2 + 0] = m_run;
+    red[(half * 128 + row) * 2 + 1] = l_run;
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(&bars->epi);
+    ok = __all_sync(0xffffffffu, ok && wait_bar(&bars->epi, 0, args.fault, FAULT_FWD_O));
+    const float m_oth = red[((1 - half) * 128 + row) * 2 + 0];
+    const float l_oth = red[((1 - half) * 128 + row) * 2 + 1];
+    const float m_a = half == 0 ? m_run : m_oth, l_a = half == 0 ? l_run : l_oth;
+    const float m_b = half == 0 ? m_oth : m_run, l_b = half == 0 ? l_oth : l_run;
+    const float m_all = fmaxf(m_a, m_b);
+    const float m_safe = m_all == -INFINITY ? 0.f : m_all;
+    const float f_a = m_a == -INFINITY ? 0.f : ptx::ex2(m_a - m_safe);
+    const float f_b = m_b == -INFINITY ? 0.f : ptx::ex2(m_b - m_safe);
+    const float l_all = l_a * f_a + l_b * f_b;
     const bool live_row = qi < p.q_len;
-    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+    const float inv = l_all > 0.f ? 1.f / l_all : 0.f;
+    const float w_a = f_a * inv, w_b = f_b * inv;
     using T = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
     T* orow = reinterpret_cast<T*>(p.o.data) + (int64_t)b * p.o.stride[0] + (int64_t)h * p.o.stride[1] +
               (int64_t)qi * p.o.stride[2];
+    // This thread writes output channels [half * D/2, half * D/2 + D/2).
 #pragma unroll
-    for (int c = 0; c < D / 32; ++c) {
-      uint32_t r[32];
+    for (int c = 0; c < D / 64; ++c) {
+      const uint32_t col = (uint32_t)(half * (D / 2) + 32 * c);
+      uint32_t ra[32], rb[32];
       if (n_tiles > 0 && ok) {
-        ptx::tmem_ld32(t_row + C::kColO + 32 * c, r);
+        ptx::tmem_ld32(t_row + C::kColO + col, ra);
+        ptx::tmem_ld32(t_row + C::kColO + D + col, rb);
         ptx::tmem_wait_ld();
       } else {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) r[e] = 0u;
+        for (int e = 0; e < 32; ++e) ra[e] = rb[e] = 0u;
       }
       if (live_row) {
+        float f[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(ra[e]) * w_a + __uint_as_float(rb[e]) * w_b;
 #pragma unroll
         for (int e = 0; e < 32; e += 8) {
           uint4 v;
-          const float* f = reinterpret_cast<const float*>(r + e);
           if (kBF16) {
-            v = make_uint4(ptx::pack_bf16(f[0] * inv, f[1] * inv), ptx::pack_bf16(f[2] * inv, f[3] * inv),
-                           ptx::pack_bf16(f[4] * inv, f[5] * inv), ptx::pack_bf16(f[6] * inv, f[7] * inv));
+            v = make_uint4(ptx::pack_bf16(f[e], f[e + 1]), ptx::pack_bf16(f[e + 2], f[e + 3]),
+                           ptx::pack_bf16(f[e + 4], f[e + 5]), ptx::pack_bf16(f[e + 6], f[e + 7]));
           } else {
-            v = make_uint4(ptx::pack_f16(f[0] * inv, f[1] * inv), ptx::pack_f16(f[2] * inv, f[3] * inv),
-                           ptx::pack_f16(f[4] * inv, f[5] * inv), ptx::pack_f16(f[6] * inv, f[7] * inv));
+            v = make_uint4(ptx::pack_f16(f[e], f[e + 1]), ptx::pack_f16(f[e + 2], f[e + 3]),
+                           ptx::pack_f16(f[e + 4], f[e + 5]), ptx::pack_f16(f[e + 6], f[e + 7]));
           }
-          *reinterpret_cast<uint4*>(orow + 32 * c + e) = v;
+          *reinterpret_cast<uint4*>(orow + col + e) = v;
         }
       }
     }
-    if (live_row && p.lse)
+    if (live_row && p.lse && half == 0)
       reinterpret_cast<float*>(p.lse)[(int64_t)b * p.lse_stride[0] + (int64_t)h * p.lse_stride[1] + (int64_t)qi * p.lse_stride[2]] =
-          l_run > 0.f ? (m_run + __log2f(l_run)) * kLn2 : -INFINITY;
+          l_all > 0.f ? (m_all + __log2f(l_all)) * kLn2 : -INFINITY;
   }
 
   ptx::tc_fence_before();
@@ -420,7 +464,7 @@ static cudaError_t launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, const
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::kSmem);
   if (e != cudaSuccess) return e;
   dim3 grid(a.n_q_tiles, a.p.q_heads, a.p.batch);
-  kern<<<grid, 256, Cfg<D>::kSmem, st>>>(mq, mk, mv, a);
+  kern<<<grid, 384, Cfg<D>::kSmem, st>>>(mq, mk, mv, a);
   return cudaGetLastError();
 }
 
