@@ -12,21 +12,24 @@
 //            (separate K and V rings so K(j+2) can land while P(j).V(j) runs)
 //   warp 1   MMA issuer (one thread): S = Q K^T into a double-buffered TMEM S,
 //            then O_A += P_A V[0:64) and O_B += P_B V[64:128) into two TMEM
-//            accumulators; completion signalled with tcgen05.commit
+//            accumulators, with P_A / P_B read from TMEM (A operand in tensor
+//            memory); completion signalled with tcgen05.commit
 //   warp 2   TMEM allocator (512 columns: S0 | S1 | O_A | O_B)
 //   warps 4-7 and 8-11: two softmax warpgroups over the same 128 rows; group
 //            A owns keys [0, 64) of every tile, group B keys [64, 128).  Thread
 //            r of a group owns query row r (TMEM lane r) and runs an
 //            independent exp2-domain online softmax over its key half (its own
 //            running max and sum, lazy rescaling of its own O accumulator when
-//            the max grows by more than 2^8), writing P (bf16/f16) into its own
-//            64-key 128B-swizzled shared slab.  The halves never synchronise in
+//            the max grows by more than 2^8), writing P (bf16/f16 pairs) back
+//            into TMEM over the S columns it just read, where the P.V MMA takes
+//            it as its A operand (no shared-memory round trip for P).  The
+//            halves never synchronise in
 //            the key loop; the epilogue merges them once:
 //            O = (O_A 2^(m_A-m) + O_B 2^(m_B-m)) / (l_A 2^(m_A-m) + l_B 2^(m_B-m)).
 //            Two warps per scheduler hide the TMEM-load and MUFU latencies that
 //            a single warpgroup of 128-key rows leaves exposed.
-// Shared-memory operands use the canonical 128-byte-swizzle layouts: Q, K and
-// P are K-major (8-row x 128-byte atoms, 1024 B apart); V is read MN-major
+// Shared-memory operands use the canonical 128-byte-swizzle layouts: Q and K
+// are K-major (8-row x 128-byte atoms, 1024 B apart); V is read MN-major
 // (64-channel blocks 16 KB apart, 8-key groups 1024 B apart).  No TMA load
 // uses cluster multicast.
 #include <type_traits>
@@ -52,8 +55,7 @@ template <int D> struct Cfg {
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + kTileBytes;
   static constexpr int kOffV = kOffK + kStages * kTileBytes;
-  static constexpr int kOffP = kOffV + kStages * kTileBytes;
-  static constexpr int kOffRed = kOffP + 2 * kSlabBytes;  // epilogue exchange [half][row][m, l]
+  static constexpr int kOffRed = kOffV + kStages * kTileBytes;  // epilogue exchange [half][row][m, l]
   static constexpr int kOffBar = kOffRed + 2 * 128 * 2 * 4;
   static constexpr int kBarBytes = 256;
   static constexpr int kSmem = kOffBar + kBarBytes + 1024;  // +1024 alignment slack
@@ -96,7 +98,6 @@ __global__ void __launch_bounds__(384, 1)
   unsigned char* sQ = smem + C::kOffQ;
   unsigned char* sK = smem + C::kOffK;
   unsigned char* sV = smem + C::kOffV;
-  unsigned char* sP = smem + C::kOffP;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q_tile = args.n_q_tiles - 1 - (int)blockIdx.x;  // longest causal tiles first
@@ -182,8 +183,7 @@ __global__ void __launch_bounds__(384, 1)
     // ------------------------------ MMA issuer ----------------------------
     if (lane == 0 && n_tiles > 0 && !dead) {
       constexpr uint32_t idesc_qk = ptx::idesc_f16(kBF16, kBM, kBN, false, false);
-      const uint32_t sQa = ptx::smem_u32(sQ), sKa = ptx::smem_u32(sK), sVa = ptx::smem_u32(sV),
-                     sPa = ptx::smem_u32(sP);
+      const uint32_t sQa = ptx::smem_u32(sQ), sKa = ptx::smem_u32(sK), sVa = ptx::smem_u32(sV);
       bool ok = wait_bar(&bars->q_full, 0, args.fault, FAULT_FWD_Q);
       ptx::tc_fence_after();
       constexpr uint32_t idesc_pv = ptx::idesc_f16(kBF16, kBM, D, false, true);
@@ -194,13 +194,14 @@ __global__ void __launch_bounds__(384, 1)
         for (int hf = 0; hf < 2; ++hf) {
           if (!wait_bar(&bars->p_full[hf], jj & 1, args.fault, FAULT_FWD_P)) return false;
           ptx::tc_fence_after();
+          // P_hf lives in TMEM over the first 32 columns of its S(jj) half (bf16x2 per column).
+          const uint32_t a_p = tmem + C::kColS + (uint32_t)(jj & 1) * kBN + hf * (kBN / 2);
 #pragma unroll
           for (int kq = 0; kq < 4; ++kq) {
             const int kk = hf * 4 + kq;
-            const uint64_t a = ptx::sw128_desc(sPa + hf * kSlabBytes + kq * 32, 16, 1024);
             const uint64_t bd =
                 ptx::sw128_desc(sVa + s * C::kTileBytes + kk * 16 * 128, kSlabBytes, 1024);
-            ptx::mma_f16_ss(tmem + C::kColO + hf * D, a, bd, idesc_pv, (jj > 0 || kq > 0) ? 1u : 0u);
+            ptx::mma_f16_ts(tmem + C::kColO + hf * D, a_p + 8 * kq, bd, idesc_pv, (jj > 0 || kq > 0) ? 1u : 0u);
           }
           ptx::mma_commit(&bars->o_done[hf]);
         }
@@ -332,7 +333,13 @@ __global__ void __launch_bounds__(384, 1)
         ptx::f2unpack(sum2[1], b0, b1);
         l_run += (a0 + a1) + (b0 + b1);
       }
-      // This half's P slab and O accumulator are free once P(j-1).V(j-1) of the half completed.
+      // P(j) into TMEM over the first 32 columns of this half's S(j) (already in
+      // registers); P(j).V(j) reads it from there, and S(j+2) only overwrites it
+      // after that MMA (one issuing thread, executed in order).
+      ptx::tmem_st32(t_row + C::kColS + (uint32_t)(j & 1) * kBN + half * kHN,
+                     pk);
+      ptx::tmem_wait_st();
+      // This half's O accumulator may be rescaled once P(j-1).V(j-1) of the half completed.
       if (j >= 1 &&
           !__all_sync(0xffffffffu, wait_bar(&bars->o_done[half], (j - 1) & 1, args.fault, FAULT_FWD_O))) {
         ok = false;
@@ -354,17 +361,6 @@ __global__ void __launch_bounds__(384, 1)
         }
         ptx::tmem_wait_st();
       }
-      // P row -> this half's 128B-swizzled K-major slab: 16-byte chunk c at (c ^ row%8).
-      {
-        unsigned char* rowp = sP + half * kSlabBytes + row * 128;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const int w = c * 4;
-          uint4 v = make_uint4(pk[w], pk[w + 1], pk[w + 2], pk[w + 3]);
-          *reinterpret_cast<uint4*>(rowp + ((c ^ (row & 7)) << 4)) = v;
-        }
-      }
-      ptx::fence_proxy_async_smem();
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&bars->p_full[half]);
