@@ -47,10 +47,11 @@ constexpr int kSlabBytes = 128 * 128;  // 128 rows x 128 bytes
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+constexpr uint32_t kFaultSmemAlign = 0x108;  // dynamic shared memory needed more alignment slack
 
 template <int D> struct Cfg {
   static constexpr int kSlabs = D / 64;
-  static constexpr int kStages = D == 64 ? 3 : 2;
+  static constexpr int kStages = 3;
   static constexpr int kTileBytes = kSlabs * kSlabBytes;  // one 128-row Q/K/V tile
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + kTileBytes;
@@ -58,7 +59,11 @@ template <int D> struct Cfg {
   static constexpr int kOffRed = kOffV + kStages * kTileBytes;  // epilogue exchange [half][row][m, l]
   static constexpr int kOffBar = kOffRed + 2 * 128 * 2 * 4;
   static constexpr int kBarBytes = 256;
-  static constexpr int kSmem = kOffBar + kBarBytes + 1024;  // +1024 alignment slack
+  // Alignment slack for the 1024-byte-aligned tile base: D=128 fills the
+  // 227 KB opt-in limit exactly, so it keeps 768 bytes and the kernel refuses
+  // to run (fault word, no access) if the dynamic window needs more.
+  static constexpr int kSlack = D == 128 ? 768 : 1024;
+  static constexpr int kSmem = kOffBar + kBarBytes + kSlack;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kColS = 0;     // two 128-column S buffers
   static constexpr uint32_t kColO = 256;   // O_A (D columns), then O_B (D columns)
@@ -92,8 +97,12 @@ __global__ void __launch_bounds__(384, 1)
   using C = Cfg<D>;
   const ts_attn_params& p = args.p;
   extern __shared__ unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t pad = (1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u;
+  if (pad > (uint32_t)C::kSlack) {  // uniform for the CTA: nothing initialised yet
+    if (threadIdx.x == 0) record_fault(args.fault, kFaultSmemAlign);
+    return;
+  }
+  unsigned char* smem = smem_raw + pad;
   Bars* bars = reinterpret_cast<Bars*>(smem + C::kOffBar);
   unsigned char* sQ = smem + C::kOffQ;
   unsigned char* sK = smem + C::kOffK;
