@@ -17,9 +17,10 @@
 //   dQ^T = K^T dS^T   [D x 64]     A = K   (MN-major) B = dS^T(MN-major)
 // P^T and dS^T are written by the "softmax" warpgroup (thread = key row) into
 // 128-byte-swizzled shared tiles that serve both as K-major A and MN-major B
-// operands.  dQ^T is read by the epilogue warpgroup (thread = channel) and
-// added into an fp32 dQ accumulator with coalesced atomics; a final kernel
-// converts it.  dK/dV stay in TMEM for the whole CTA (no atomics, GQA summed).
+// operands.  dQ^T is read by the epilogue warpgroup (thread = channel),
+// staged row-major in shared memory and added into an fp32 dQ accumulator with
+// one bulk reduce-add (cp.reduce.async.bulk .add.f32) per query tile; a final
+// kernel converts it.  dK/dV stay in TMEM for the whole CTA (no atomics, GQA summed).
 //
 // Warps: 0 TMA producer, 1 MMA issuer, 2 TMEM allocator, 4-7 softmax
 // (P^T, dS^T, then the dK/dV epilogue), 8-11 dQ epilogue.  No TMA load uses
@@ -50,7 +51,8 @@ template <int D> struct BwdCfg {
   static constexpr int kOffP = kOffDO + 2 * kSlabs * kQSlab;
   static constexpr int kOffDS = kOffP + kKSlab;
   static constexpr int kOffStat = kOffDS + kKSlab;             // [2][2][64] floats
-  static constexpr int kOffBar = kOffStat + 2 * 2 * kBM * 4;
+  static constexpr int kOffDQ = kOffStat + 2 * 2 * kBM * 4;     // [2][64][D] fp32 dQ staging
+  static constexpr int kOffBar = kOffDQ + 2 * kBM * D * 4;
   static constexpr int kUsed = kOffBar + 256 + 1024;
   // One CTA per SM: the kernel owns all 512 TMEM columns.
   static constexpr int kSmem = kUsed > 120 * 1024 ? kUsed : 120 * 1024;
@@ -260,7 +262,13 @@ __global__ void __launch_bounds__(384, 1)
       if (ok) {
         ptx::tc_fence_after();
         const bool key_ok = key < kv_end;
-#pragma unroll
+        // Query columns this key row is visible to: col >= c_min (causal rule
+        // i + offset >= key), none when the key is past the row's end.
+        const int64_t cm = p.is_causal ? (int64_t)key - offset - q0 : 0;
+        const int c_min = key_ok ? (int)i64max(0, i64min(kBM, cm)) : kBM;
+        // Not unrolled over the two halves: one copy of the element loop keeps
+        // the softmax warps' code small next to the other roles' code.
+#pragma unroll 1
         for (int half = 0; half < 2; ++half) {
           uint32_t rs[32], rd[32];
           ptx::tmem_ld32(t_row + C::kColS + 32 * half, rs);
@@ -272,17 +280,23 @@ __global__ void __launch_bounds__(384, 1)
             if (lane == 0) ptx::mbar_arrive(&bars->s_free);
           }
           uint32_t pk[16], dk[16];
+          float lv[32], dl[32];  // this half's LSE (log2 units) and delta, broadcast from shared memory
+#pragma unroll
+          for (int c = 0; c < 32; c += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(lse2 + 32 * half + c);
+            const float4 d4 = *reinterpret_cast<const float4*>(dlt + 32 * half + c);
+            lv[c] = a.x, lv[c + 1] = a.y, lv[c + 2] = a.z, lv[c + 3] = a.w;
+            dl[c] = d4.x, dl[c + 1] = d4.y, dl[c + 2] = d4.z, dl[c + 3] = d4.w;
+          }
 #pragma unroll
           for (int c = 0; c < 32; c += 2) {
             float pv[2], dsv[2];
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
               const int col = 32 * half + c + e;
-              const int64_t i = q0 + col;
-              const bool vis = key_ok && (!p.is_causal || i + offset >= key);
-              const float pr = vis ? ptx::ex2(__uint_as_float(rs[c + e]) * sl2 - lse2[col]) : 0.f;
+              const float pr = col >= c_min ? ptx::ex2(fmaf(__uint_as_float(rs[c + e]), sl2, -lv[c + e])) : 0.f;
               pv[e] = pr;
-              dsv[e] = pr * (__uint_as_float(rd[c + e]) - dlt[col]) * scale;
+              dsv[e] = (pr * scale) * (__uint_as_float(rd[c + e]) - dl[c + e]);
             }
             pk[c / 2] = kBF16 ? ptx::pack_bf16(pv[0], pv[1]) : ptx::pack_f16(pv[0], pv[1]);
             dk[c / 2] = kBF16 ? ptx::pack_bf16(dsv[0], dsv[1]) : ptx::pack_f16(dsv[0], dsv[1]);
@@ -352,34 +366,49 @@ __global__ void __launch_bounds__(384, 1)
     }
   } else if (warp >= 8) {
     // ----------------------- dQ epilogue (thread = channel) ----------------
+    // dQ^T (lane = channel) -> a row-major [64][D] fp32 staging tile (double
+    // buffered) -> one bulk reduce-add into the fp32 dQ accumulator per
+    // iteration, issued by the group's first thread.  Every dQ warp runs all
+    // n_it iterations and reaches both named barriers; after a failed wait it
+    // only skips the work.
     const int d = (warp - 8) * 32 + lane;
+    const bool leader = threadIdx.x == 256;
     const uint32_t t_row = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    float* stage = reinterpret_cast<float*>(smem + C::kOffDQ);
     bool ok = !dead;
-    for (int it = 0; it < n_it && ok; ++it) {
-      if (!__all_sync(0xffffffffu, wait_bar(&bars->b_done, it & 1, args.fault, FAULT_FWD_O))) {
-        ok = false;
-        break;
-      }
-      ptx::tc_fence_after();
+    for (int it = 0; it < n_it; ++it) {
+      if (ok) ok = __all_sync(0xffffffffu, wait_bar(&bars->b_done, it & 1, args.fault, FAULT_FWD_O));
       uint32_t r0[32], r1[32];
-      ptx::tmem_ld32(t_row + C::kColDQ, r0);
-      ptx::tmem_ld32(t_row + C::kColDQ + 32, r1);
-      ptx::tmem_wait_ld();
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&bars->dq_free);
-      if (d < D) {
+      if (ok) {
+        ptx::tc_fence_after();
+        ptx::tmem_ld32(t_row + C::kColDQ, r0);
+        ptx::tmem_ld32(t_row + C::kColDQ + 32, r1);
+        ptx::tmem_wait_ld();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&bars->dq_free);
+      }
+      // Staging buffer it&1 is free once the reduce issued two iterations ago read it.
+      if (leader) ptx::bulk_wait_read<1>();
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+      float* st = stage + (it & 1) * kBM * D;
+      if (ok && d < D) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) st[c * D + d] = __uint_as_float(r0[c]);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) st[(32 + c) * D + d] = __uint_as_float(r1[c]);
+      }
+      ptx::fence_proxy_async_smem();
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+      if (leader && ok) {
         const int h = it_head(it), q0 = it_q0(it);
-        float* acc = args.dq_acc + (((int64_t)b * p.q_heads + h) * p.q_len + q0) * D + d;
         const int rows = min(kBM, p.q_len - q0);
-#pragma unroll
-        for (int c = 0; c < 32; ++c)
-          if (c < rows) atomicAdd(acc + (int64_t)c * D, __uint_as_float(r0[c]));
-#pragma unroll
-        for (int c = 0; c < 32; ++c)
-          if (32 + c < rows) atomicAdd(acc + (int64_t)(32 + c) * D, __uint_as_float(r1[c]));
+        ptx::bulk_reduce_add_f32(args.dq_acc + (((int64_t)b * p.q_heads + h) * p.q_len + q0) * D, st,
+                                 (uint32_t)(rows * D * 4));
+        ptx::bulk_commit();
       }
     }
+    if (leader) ptx::bulk_wait_all();
   }
 
   ptx::tc_fence_before();
