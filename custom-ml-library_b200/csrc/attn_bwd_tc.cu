@@ -38,6 +38,7 @@ namespace {
 
 constexpr int kBN = 128;  // keys per CTA
 constexpr int kBM = 64;   // query rows per iteration
+constexpr int kQStages = 3;  // Q / dO / row-statistics ring depth
 constexpr int kKSlab = 128 * 128;  // 128 rows x 128 B
 constexpr int kQSlab = 64 * 128;   // 64 rows x 128 B
 constexpr float kLog2e = 1.4426950408889634f;
@@ -46,13 +47,13 @@ template <int D> struct BwdCfg {
   static constexpr int kSlabs = D / 64;
   static constexpr int kOffK = 0;
   static constexpr int kOffV = kOffK + kSlabs * kKSlab;
-  static constexpr int kOffQ = kOffV + kSlabs * kKSlab;       // 2 stages
-  static constexpr int kOffDO = kOffQ + 2 * kSlabs * kQSlab;   // 2 stages
-  static constexpr int kOffP = kOffDO + 2 * kSlabs * kQSlab;
+  static constexpr int kOffQ = kOffV + kSlabs * kKSlab;                // kQStages stages
+  static constexpr int kOffDO = kOffQ + kQStages * kSlabs * kQSlab;     // kQStages stages
+  static constexpr int kOffP = kOffDO + kQStages * kSlabs * kQSlab;
   static constexpr int kOffDS = kOffP + kKSlab;
-  static constexpr int kOffStat = kOffDS + kKSlab;             // [2][2][64] floats
-  static constexpr int kOffDQ = kOffStat + 2 * 2 * kBM * 4;     // [2][64][D] fp32 dQ staging
-  static constexpr int kOffBar = kOffDQ + 2 * kBM * D * 4;
+  static constexpr int kOffStat = kOffDS + kKSlab;             // [stage][-LSE*log2e | -delta][64] floats
+  static constexpr int kOffDQ = kOffStat + kQStages * 2 * kBM * 4;  // [64][D] fp32 dQ staging
+  static constexpr int kOffBar = kOffDQ + kBM * D * 4;
   static constexpr int kUsed = kOffBar + 256 + 1024;
   // One CTA per SM: the kernel owns all 512 TMEM columns.
   static constexpr int kSmem = kUsed > 120 * 1024 ? kUsed : 120 * 1024;
@@ -61,7 +62,7 @@ template <int D> struct BwdCfg {
 
 struct BwdBars {
   uint64_t kv_full;
-  uint64_t qdo_full[2], qdo_empty[2];
+  uint64_t qdo_full[kQStages], qdo_empty[kQStages];
   uint64_t s_full, s_free, p_full, b_done, dq_free, drain;
   uint32_t tmem_base;
 };
@@ -69,7 +70,8 @@ struct BwdBars {
 struct TcBwdArgs {
   ts_attn_params p;  // forward problem (q, k, v, o, lse)
   ts_view4 dk, dv;
-  float* delta;      // [B, Hq, Tq]
+  float* stats;      // [B*Hq][2][t_pad]: -LSE*log2e (-inf: no row / fully masked), -delta (0: no row)
+  int t_pad;         // Tq rounded up to the 64-row query tile
   float* dq_acc;     // [B, Hq, Tq, D]
   int n_k_tiles;
   uint32_t* fault;
@@ -117,7 +119,7 @@ __global__ void __launch_bounds__(384, 1)
 
   if (threadIdx.x == 0) {
     ptx::mbar_init(&bars->kv_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kQStages; ++s) {
       ptx::mbar_init(&bars->qdo_full[s], 1);
       ptx::mbar_init(&bars->qdo_empty[s], 1);
     }
@@ -155,19 +157,24 @@ __global__ void __launch_bounds__(384, 1)
       }
       int issued = 0;
       for (int it = 0; it < n_it; ++it) {
-        const int s = it & 1;
-        if (it >= 2 && !wait_bar(&bars->qdo_empty[s], ((it >> 1) - 1) & 1, args.fault, FAULT_FWD_EMPTY)) break;
+        const int s = it % kQStages;
+        if (it >= kQStages && !wait_bar(&bars->qdo_empty[s], ((it / kQStages) - 1) & 1, args.fault, FAULT_FWD_EMPTY))
+          break;
         const int h = it_head(it), q0 = it_q0(it);
-        ptx::mbar_expect_tx(&bars->qdo_full[s], 2 * C::kSlabs * kQSlab);
+        ptx::mbar_expect_tx(&bars->qdo_full[s], 2 * C::kSlabs * kQSlab + 2 * kBM * 4);
         for (int sl = 0; sl < C::kSlabs; ++sl) {
           ptx::tma_load_4d(sQ + (s * C::kSlabs + sl) * kQSlab, &tm_q, 64 * sl, q0, h, b, &bars->qdo_full[s]);
           ptx::tma_load_4d(sDO + (s * C::kSlabs + sl) * kQSlab, &tm_do, 64 * sl, q0, h, b, &bars->qdo_full[s]);
         }
+        // The tile's row statistics (padded rows: p = 0, delta = 0) ride on the same barrier.
+        const float* st = args.stats + ((int64_t)b * p.q_heads + h) * 2 * args.t_pad + q0;
+        ptx::bulk_g2s(sStat + s * 2 * kBM, st, kBM * 4, &bars->qdo_full[s]);
+        ptx::bulk_g2s(sStat + s * 2 * kBM + kBM, st + args.t_pad, kBM * 4, &bars->qdo_full[s]);
         issued = it + 1;
       }
       (void)wait_bar(&bars->kv_full, 0, nullptr, FAULT_FWD_DRAIN);
-      for (int it = max(0, issued - 2); it < issued; ++it)
-        (void)wait_bar(&bars->qdo_full[it & 1], (it >> 1) & 1, nullptr, FAULT_FWD_DRAIN);
+      for (int it = max(0, issued - kQStages); it < issued; ++it)
+        (void)wait_bar(&bars->qdo_full[it % kQStages], (it / kQStages) & 1, nullptr, FAULT_FWD_DRAIN);
     }
   } else if (warp == 1) {
     // ------------------------------ MMA issuer ----------------------------
@@ -179,8 +186,8 @@ __global__ void __launch_bounds__(384, 1)
                      aDO = ptx::smem_u32(sDO), aP = ptx::smem_u32(sP), aDS = ptx::smem_u32(sDS);
       bool ok = wait_bar(&bars->kv_full, 0, args.fault, FAULT_FWD_KV);
       auto issue_a = [&](int it) -> bool {
-        const int s = it & 1;
-        if (!wait_bar(&bars->qdo_full[s], (it >> 1) & 1, args.fault, FAULT_FWD_KV)) return false;
+        const int s = it % kQStages;
+        if (!wait_bar(&bars->qdo_full[s], (it / kQStages) & 1, args.fault, FAULT_FWD_KV)) return false;
         ptx::tc_fence_after();
         const uint32_t q = aQ + s * C::kSlabs * kQSlab, dO = aDO + s * C::kSlabs * kQSlab;
 #pragma unroll
@@ -208,7 +215,7 @@ __global__ void __launch_bounds__(384, 1)
           break;
         }
         ptx::tc_fence_after();
-        const int s = it & 1;
+        const int s = it % kQStages;
         const uint32_t q = aQ + s * C::kSlabs * kQSlab, dO = aDO + s * C::kSlabs * kQSlab;
 #pragma unroll
         for (int kk = 0; kk < kBM / 16; ++kk) {
@@ -235,30 +242,16 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t t_row = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const float sl2 = (float)p.scale * kLog2e, scale = (float)p.scale;
     bool ok = !dead;
-    // Row statistics of iteration `it` (thread t < 64: LSE of row t; else delta of row t-64).
-    auto stat_value = [&](int it) -> float {
-      const int h = it_head(it), q0 = it_q0(it);
-      const int t = row & 63, i = q0 + t;
-      if (row < 64) {
-        if (i >= p.q_len) return INFINITY;
-        const float l = reinterpret_cast<const float*>(p.lse)[(int64_t)b * p.lse_stride[0] +
-                                                              (int64_t)h * p.lse_stride[1] +
-                                                              (int64_t)i * p.lse_stride[2]];
-        return l == -INFINITY ? INFINITY : l * kLog2e;  // fully masked row -> p = 0
-      }
-      return i < p.q_len ? args.delta[((int64_t)b * p.q_heads + h) * p.q_len + i] : 0.f;
-    };
-    if (n_it > 0) sStat[row] = stat_value(0);
-    asm volatile("bar.sync 1, 128;" ::: "memory");
     // Every softmax warp runs all n_it iterations and reaches every named
     // barrier; after a failed wait it only skips the work (no early exit).
     for (int it = 0; it < n_it; ++it) {
       const int q0 = it_q0(it);
-      const float next = (it + 1 < n_it) ? stat_value(it + 1) : 0.f;
-      const float* lse2 = sStat + (it & 1) * 128;
-      const float* dlt = lse2 + 64;
-      // Warp-uniform outcomes: the tcgen05.ld below are warp-collective.
-      if (ok) ok = __all_sync(0xffffffffu, wait_bar(&bars->s_full, it & 1, args.fault, FAULT_FWD_S));
+      const float* nlse2 = sStat + (it % kQStages) * 2 * kBM;
+      const float* ndlt = nlse2 + kBM;
+      // Warp-uniform outcomes: the tcgen05.ld below are warp-collective.  The
+      // statistics landed with the Q/dO stage (already complete when S is).
+      if (ok) ok = __all_sync(0xffffffffu, wait_bar(&bars->qdo_full[it % kQStages], (it / kQStages) & 1, args.fault, FAULT_FWD_KV) &&
+                                               wait_bar(&bars->s_full, it & 1, args.fault, FAULT_FWD_S));
       if (ok) {
         ptx::tc_fence_after();
         const bool key_ok = key < kv_end;
@@ -280,26 +273,39 @@ __global__ void __launch_bounds__(384, 1)
             if (lane == 0) ptx::mbar_arrive(&bars->s_free);
           }
           uint32_t pk[16], dk[16];
-          float lv[32], dl[32];  // this half's LSE (log2 units) and delta, broadcast from shared memory
+          // This half's -LSE*log2e and -delta as packed pairs (float4 broadcasts from shared memory).
+          uint64_t nl2[16], nd2[16];
 #pragma unroll
           for (int c = 0; c < 32; c += 4) {
-            const float4 a = *reinterpret_cast<const float4*>(lse2 + 32 * half + c);
-            const float4 d4 = *reinterpret_cast<const float4*>(dlt + 32 * half + c);
-            lv[c] = a.x, lv[c + 1] = a.y, lv[c + 2] = a.z, lv[c + 3] = a.w;
-            dl[c] = d4.x, dl[c + 1] = d4.y, dl[c + 2] = d4.z, dl[c + 3] = d4.w;
+            const float4 a = *reinterpret_cast<const float4*>(nlse2 + 32 * half + c);
+            const float4 d4 = *reinterpret_cast<const float4*>(ndlt + 32 * half + c);
+            nl2[c / 2] = ptx::f2pack(a.x, a.y), nl2[c / 2 + 1] = ptx::f2pack(a.z, a.w);
+            nd2[c / 2] = ptx::f2pack(d4.x, d4.y), nd2[c / 2 + 1] = ptx::f2pack(d4.z, d4.w);
           }
+          // Columns below c_min are masked; warp-uniform fast path when none of this half is.
+          const bool all_vis = __all_sync(0xffffffffu, c_min <= 32 * half);
+          const uint64_t sl2x2 = ptx::f2pack(sl2, sl2), scx2 = ptx::f2pack(scale, scale);
 #pragma unroll
           for (int c = 0; c < 32; c += 2) {
-            float pv[2], dsv[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int col = 32 * half + c + e;
-              const float pr = col >= c_min ? ptx::ex2(fmaf(__uint_as_float(rs[c + e]), sl2, -lv[c + e])) : 0.f;
-              pv[e] = pr;
-              dsv[e] = (pr * scale) * (__uint_as_float(rd[c + e]) - dl[c + e]);
+            // p = exp2(s * scale * log2e - LSE * log2e); dS = p * scale * (dP - delta), in f32 pairs.
+            const uint64_t x2 = ptx::fma2(ptx::f2pack(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), sl2x2,
+                                          nl2[c / 2]);
+            float x0, x1;
+            ptx::f2unpack(x2, x0, x1);
+            float p0 = ptx::ex2(x0), p1 = ptx::ex2(x1);
+            if (!all_vis) {
+              const int col = 32 * half + c;
+              p0 = col >= c_min ? p0 : 0.f;
+              p1 = col + 1 >= c_min ? p1 : 0.f;
             }
-            pk[c / 2] = kBF16 ? ptx::pack_bf16(pv[0], pv[1]) : ptx::pack_f16(pv[0], pv[1]);
-            dk[c / 2] = kBF16 ? ptx::pack_bf16(dsv[0], dsv[1]) : ptx::pack_f16(dsv[0], dsv[1]);
+            const uint64_t p2 = ptx::f2pack(p0, p1);
+            const uint64_t t2 =
+                ptx::add2(ptx::f2pack(__uint_as_float(rd[c]), __uint_as_float(rd[c + 1])), nd2[c / 2]);
+            const uint64_t ds2 = ptx::fma2(ptx::fma2(p2, scx2, 0ull), t2, 0ull);
+            float d0, d1;
+            ptx::f2unpack(ds2, d0, d1);
+            pk[c / 2] = kBF16 ? ptx::pack_bf16(p0, p1) : ptx::pack_f16(p0, p1);
+            dk[c / 2] = kBF16 ? ptx::pack_bf16(d0, d1) : ptx::pack_f16(d0, d1);
           }
           // P^T / dS^T buffers are free once the previous iteration's dV/dK/dQ MMAs completed.
           if (half == 0 && it >= 1)
@@ -323,8 +329,6 @@ __global__ void __launch_bounds__(384, 1)
           if (lane == 0) ptx::mbar_arrive(&bars->p_full);
         }
       }
-      sStat[((it + 1) & 1) * 128 + row] = next;
-      asm volatile("bar.sync 1, 128;" ::: "memory");
     }
     // dK / dV epilogue: TMEM rows -> global.
     if (ok && n_it > 0)
@@ -366,8 +370,8 @@ __global__ void __launch_bounds__(384, 1)
     }
   } else if (warp >= 8) {
     // ----------------------- dQ epilogue (thread = channel) ----------------
-    // dQ^T (lane = channel) -> a row-major [64][D] fp32 staging tile (double
-    // buffered) -> one bulk reduce-add into the fp32 dQ accumulator per
+    // dQ^T (lane = channel) -> a row-major [64][D] fp32 staging tile -> one
+    // bulk reduce-add into the fp32 dQ accumulator per
     // iteration, issued by the group's first thread.  Every dQ warp runs all
     // n_it iterations and reaches both named barriers; after a failed wait it
     // only skips the work.
@@ -388,10 +392,10 @@ __global__ void __launch_bounds__(384, 1)
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&bars->dq_free);
       }
-      // Staging buffer it&1 is free once the reduce issued two iterations ago read it.
-      if (leader) ptx::bulk_wait_read<1>();
+      // The staging tile is free once the previous iteration's reduce has read it.
+      if (leader) ptx::bulk_wait_read<0>();
       asm volatile("bar.sync 2, 128;" ::: "memory");
-      float* st = stage + (it & 1) * kBM * D;
+      float* st = stage;
       if (ok && d < D) {
 #pragma unroll
         for (int c = 0; c < 32; ++c) st[c * D + d] = __uint_as_float(r0[c]);
@@ -454,10 +458,48 @@ bool tc_bwd_supported(const ts_attn_bwd_params& bp) {
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+static int t_padded(int q_len) { return ceil_div(q_len, kBM) * kBM; }
+
 size_t tc_bwd_workspace(const ts_attn_bwd_params& bp) {
   const ts_attn_params& p = bp.fwd;
   const size_t rows = (size_t)p.batch * p.q_heads * p.q_len;
-  return align256(rows * sizeof(float)) + align256(rows * p.head_dim * sizeof(float));
+  const size_t stats = (size_t)p.batch * p.q_heads * 2 * t_padded(p.q_len);
+  return align256(stats * sizeof(float)) + align256(rows * p.head_dim * sizeof(float));
+}
+
+// stats[bh][0][i] = -LSE*log2e (-inf for a fully masked row or i >= Tq) and
+// stats[bh][1][i] = -sum_c dO*O (0 for i >= Tq): the backward's row statistics
+// (nn/attention.py:231), one warp per padded row.
+template <typename T>
+__global__ void bwd_stats_kernel(ts_attn_bwd_params bp, float* stats, int t_pad) {
+  const ts_attn_params& p = bp.fwd;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t total = (int64_t)p.batch * p.q_heads * t_pad;
+  if (warp >= total) return;
+  const int i = (int)(warp % t_pad);
+  const int64_t bh = warp / t_pad;
+  const int h = (int)(bh % p.q_heads), b = (int)(bh / p.q_heads);
+  float acc = 0.f;
+  if (i < p.q_len) {
+    const T* g = reinterpret_cast<const T*>(bp.dout.data) + b * bp.dout.stride[0] + h * bp.dout.stride[1] +
+                 i * bp.dout.stride[2];
+    const T* o = reinterpret_cast<const T*>(p.o.data) + b * p.o.stride[0] + h * p.o.stride[1] + i * p.o.stride[2];
+    for (int c = lane; c < p.value_dim; c += 32)
+      acc += Elem<T>::to_acc(g[c * bp.dout.stride[3]]) * Elem<T>::to_acc(o[c * p.o.stride[3]]);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    float nl = -INFINITY;
+    if (i < p.q_len) {
+      const float l = reinterpret_cast<const float*>(p.lse)[(int64_t)b * p.lse_stride[0] +
+                                                            (int64_t)h * p.lse_stride[1] + (int64_t)i * p.lse_stride[2]];
+      nl = l == -INFINITY ? -INFINITY : -l * kLog2e;
+    }
+    stats[bh * 2 * t_pad + i] = nl;
+    stats[bh * 2 * t_pad + t_pad + i] = i < p.q_len ? -acc : 0.f;
+  }
 }
 
 template <int D, bool BF16>
@@ -476,15 +518,25 @@ cudaError_t tc_backward(const ts_attn_bwd_params& bp, void* ws, size_t ws_bytes,
   const ts_attn_params& p = bp.fwd;
   if (ws_bytes < tc_bwd_workspace(bp)) return cudaErrorInvalidValue;
   const size_t rows = (size_t)p.batch * p.q_heads * p.q_len;
-  float* delta = reinterpret_cast<float*>(ws);
-  float* dq_acc = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(ws) + align256(rows * sizeof(float)));
+  const int t_pad = t_padded(p.q_len);
+  const size_t n_stats = (size_t)p.batch * p.q_heads * 2 * t_pad;
+  float* stats = reinterpret_cast<float*>(ws);
+  float* dq_acc = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(ws) + align256(n_stats * sizeof(float)));
   CUtensorMap mq, mk, mv, mdo;
   if (!make_map(&mq, p.q, p.dtype, p.batch, p.q_heads, p.q_len, p.head_dim, kBM) ||
       !make_map(&mk, p.k, p.dtype, p.batch, p.kv_heads, p.kv_len, p.head_dim, kBN) ||
       !make_map(&mv, p.v, p.dtype, p.batch, p.kv_heads, p.kv_len, p.value_dim, kBN) ||
       !make_map(&mdo, bp.dout, p.dtype, p.batch, p.q_heads, p.q_len, p.value_dim, kBM))
     return cudaErrorInvalidValue;
-  cudaError_t e = simt_delta_f32(bp, delta, st);
+  {
+    const int64_t warps = (int64_t)p.batch * p.q_heads * t_pad;
+    const unsigned blocks = (unsigned)((warps * 32 + 255) / 256);
+    if (p.dtype == TS_BF16)
+      bwd_stats_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(bp, stats, t_pad);
+    else
+      bwd_stats_kernel<__half><<<blocks, 256, 0, st>>>(bp, stats, t_pad);
+  }
+  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   e = cudaMemsetAsync(dq_acc, 0, rows * p.head_dim * sizeof(float), st);
   if (e != cudaSuccess) return e;
@@ -492,7 +544,8 @@ cudaError_t tc_backward(const ts_attn_bwd_params& bp, void* ws, size_t ws_bytes,
   a.p = p;
   a.dk = bp.dk;
   a.dv = bp.dv;
-  a.delta = delta;
+  a.stats = stats;
+  a.t_pad = t_pad;
   a.dq_acc = dq_acc;
   a.n_k_tiles = ceil_div(p.kv_len, kBN);
   a.fault = fault;
