@@ -566,12 +566,12 @@ def run_c3(args):
                    "l2": "inputs larger than L2 (0.7 GB per step)"},
         "forward": {"tflops": fwd_tf, "ms": fwd, "frac_of_measured_bf16": fwd_tf / peaks["bf16_tflops"]},
         "backward": {"tflops": bwd_tf, "ms": bwd, "frac_of_measured_bf16": bwd_tf / peaks["bf16_tflops"],
-                     "launches": "delta preprocess + dQ zero + tc_bwd_kernel + dQ convert"},
+                     "launches": "row-statistics preprocess + dQ accumulator memset + tc_bwd_kernel + dQ convert"},
         "roofline": {"bound": "tensor", "kernel": "backward call (tc_bwd_kernel dominant)", "achieved": bwd_tf,
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": bwd_tf / peaks["bf16_tflops"],
                      "peak_source": f"{src} bf16_tflops (burst; the call runs ~ms)", "traffic": None,
                      "algorithmic": f"10*D*causal_pairs = {10 * pairs_flops:.4g} FLOP per backward call"},
-        "gpu_launches": 5 * args.steps,
+        "gpu_launches": 4 * args.steps,  # tc_fwd_kernel, bwd_stats_kernel, tc_bwd_kernel, dq_convert_kernel
         "clocks": clocks,
     }
     if not args.no_cpu_baseline:

@@ -10,17 +10,21 @@
 // of every query head of the group (causal: only tiles that see the keys).
 // Per query tile five MMAs run with TMEM accumulators (lane = key for the
 // first four, lane = channel for the last):
-//   S^T  = K  Q^T     [128 x 64]   A = K   (K-major)  B = Q   (K-major)
-//   dP^T = V  dO^T    [128 x 64]   A = V   (K-major)  B = dO  (K-major)
-//   dV  += P^T dO     [128 x Dv]   A = P^T (K-major)  B = dO  (MN-major)
-//   dK  += dS^T Q     [128 x D]    A = dS^T(K-major)  B = Q   (MN-major)
-//   dQ^T = K^T dS^T   [D x 64]     A = K   (MN-major) B = dS^T(MN-major)
-// P^T and dS^T are written by the "softmax" warpgroup (thread = key row) into
-// 128-byte-swizzled shared tiles that serve both as K-major A and MN-major B
-// operands.  dQ^T is read by the epilogue warpgroup (thread = channel),
-// staged row-major in shared memory and added into an fp32 dQ accumulator with
-// one bulk reduce-add (cp.reduce.async.bulk .add.f32) per query tile; a final
-// kernel converts it.  dK/dV stay in TMEM for the whole CTA (no atomics, GQA summed).
+//   S^T  = K  Q^T     [128 x 64]   A = K   (smem, K-major)  B = Q   (K-major)
+//   dP^T = V  dO^T    [128 x 64]   A = V   (smem, K-major)  B = dO  (K-major)
+//   dV  += P^T dO     [128 x Dv]   A = P^T (TMEM)           B = dO  (MN-major)
+//   dK  += dS^T Q     [128 x D]    A = dS^T(TMEM)           B = Q   (MN-major)
+//   dQ^T = K^T dS^T   [D x 64]     A = K   (smem, MN-major) B = dS^T(smem, MN-major)
+// The "softmax" warpgroup (thread = key row) forms P^T and dS^T from S^T, dP^T
+// and the tile's row statistics, and writes them as bf16/f16 pairs into TMEM
+// (A operands of dV / dK) and dS^T also into a 128-byte-swizzled shared tile
+// (B operand of dQ^T).  Row statistics (-LSE*log2e, -delta, padded to the
+// 64-row tile) are written by a small preprocess kernel and copied by the
+// producer beside each Q/dO tile (3-stage ring).  dQ^T is read by the epilogue
+// warpgroup (thread = channel), staged row-major in shared memory and added
+// into an fp32 dQ accumulator with one bulk reduce-add (cp.reduce.async.bulk
+// .add.f32) per query tile; a final kernel converts it.  dK/dV stay in TMEM
+// for the whole CTA (no atomics, GQA summed).
 //
 // Warps: 0 TMA producer, 1 MMA issuer, 2 TMEM allocator, 4-7 softmax
 // (P^T, dS^T, then the dK/dV epilogue), 8-11 dQ epilogue.  No TMA load uses
@@ -58,6 +62,8 @@ template <int D> struct BwdCfg {
   // One CTA per SM: the kernel owns all 512 TMEM columns.
   static constexpr int kSmem = kUsed > 120 * 1024 ? kUsed : 120 * 1024;
   static constexpr uint32_t kColDK = 0, kColDV = 128, kColS = 256, kColDP = 320, kColDQ = 384;
+  // P^T and dS^T as bf16/f16 pairs (A operands of dV / dK read from TMEM).
+  static constexpr uint32_t kColP = 448, kColDSt = 480;
 };
 
 struct BwdBars {
@@ -95,7 +101,6 @@ __global__ void __launch_bounds__(384, 1)
   unsigned char* sV = smem + C::kOffV;
   unsigned char* sQ = smem + C::kOffQ;
   unsigned char* sDO = smem + C::kOffDO;
-  unsigned char* sP = smem + C::kOffP;
   unsigned char* sDS = smem + C::kOffDS;
   float* sStat = reinterpret_cast<float*>(smem + C::kOffStat);  // [buf][lse2 | delta][64]
 
@@ -183,7 +188,7 @@ __global__ void __launch_bounds__(384, 1)
       constexpr uint32_t id_dkv = ptx::idesc_f16(kBF16, 128, D, false, true);
       constexpr uint32_t id_dq = ptx::idesc_f16(kBF16, 128, kBM, true, true);
       const uint32_t aK = ptx::smem_u32(sK), aV = ptx::smem_u32(sV), aQ = ptx::smem_u32(sQ),
-                     aDO = ptx::smem_u32(sDO), aP = ptx::smem_u32(sP), aDS = ptx::smem_u32(sDS);
+                     aDO = ptx::smem_u32(sDO), aDS = ptx::smem_u32(sDS);
       bool ok = wait_bar(&bars->kv_full, 0, args.fault, FAULT_FWD_KV);
       auto issue_a = [&](int it) -> bool {
         const int s = it % kQStages;
@@ -220,9 +225,9 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
         for (int kk = 0; kk < kBM / 16; ++kk) {
           const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
-          ptx::mma_f16_ss(tmem + C::kColDV, ptx::sw128_desc(aP + kk * 32, 16, 1024),
+          ptx::mma_f16_ts(tmem + C::kColDV, tmem + C::kColP + kk * 8,
                           ptx::sw128_desc(dO + kk * 16 * 128, kQSlab, 1024), id_dkv, acc);
-          ptx::mma_f16_ss(tmem + C::kColDK, ptx::sw128_desc(aDS + kk * 32, 16, 1024),
+          ptx::mma_f16_ts(tmem + C::kColDK, tmem + C::kColDSt + kk * 8,
                           ptx::sw128_desc(q + kk * 16 * 128, kQSlab, 1024), id_dkv, acc);
         }
 #pragma unroll
@@ -311,18 +316,21 @@ __global__ void __launch_bounds__(384, 1)
           if (half == 0 && it >= 1)
             ok = __all_sync(0xffffffffu, wait_bar(&bars->b_done, (it - 1) & 1, args.fault, FAULT_FWD_O));
           if (ok) {
+            // P^T and dS^T into TMEM (A operands of dV += P^T dO, dK += dS^T Q);
+            // dS^T also into the swizzled shared tile, the B operand of dQ^T.
+            ptx::tmem_st16(t_row + C::kColP + 16 * half, pk);
+            ptx::tmem_st16(t_row + C::kColDSt + 16 * half, dk);
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
               const int chunk = half * 4 + c;
               const int off = row * 128 + ((chunk ^ (row & 7)) << 4);
-              *reinterpret_cast<uint4*>(sP + off) =
-                  make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
               *reinterpret_cast<uint4*>(sDS + off) =
                   make_uint4(dk[4 * c], dk[4 * c + 1], dk[4 * c + 2], dk[4 * c + 3]);
             }
           }
         }
         if (ok) {
+          ptx::tmem_wait_st();
           ptx::fence_proxy_async_smem();
           ptx::tc_fence_before();
           __syncwarp();
