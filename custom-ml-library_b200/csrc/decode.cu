@@ -397,12 +397,14 @@ bool decode_supported(const ts_attn_params& p) {
 }
 
 static int decode_split_keys(const ts_attn_params& p, int sm_count) {
-  // Aim for about 16 waves of 3 CTAs per SM over the longest-row estimate.
+  // Aim for about 4 waves of 3 CTAs per SM over the longest-row estimate, with
+  // at least 512 keys (16 chunks) per split: short splits spend their time
+  // filling the 4-stage ring, too few waves leave ragged rows unbalanced.
   const int64_t keys = (int64_t)p.batch * p.kv_heads * p.kv_len;
-  const int64_t target_ctas = (int64_t)sm_count * 3 * 16;
+  const int64_t target_ctas = (int64_t)sm_count * 3 * 4;
   int64_t s = (keys + target_ctas - 1) / target_ctas;
   s = ((s + kDecChunk - 1) / kDecChunk) * kDecChunk;
-  s = s < 256 ? 256 : (s > 8192 ? 8192 : s);
+  s = s < 512 ? 512 : (s > 8192 ? 8192 : s);
   return (int)s;
 }
 

@@ -433,10 +433,10 @@ static int int8_split_keys(const ts_attn_params& p) {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t keys = (int64_t)p.batch * p.kv_heads * p.kv_len;
-  const int64_t target = (int64_t)sms * 4 * 16;
+  const int64_t target = (int64_t)sms * 6 * 4;  // about 4 waves, at least 512 keys per split (see decode.cu)
   int64_t s = (keys + target - 1) / target;
   s = ((s + kChunk - 1) / kChunk) * kChunk;
-  return (int)(s < 256 ? 256 : (s > 8192 ? 8192 : s));
+  return (int)(s < 512 ? 512 : (s > 8192 ? 8192 : s));
 }
 
 size_t decode_int8_workspace(const ts_attn_params& p) {

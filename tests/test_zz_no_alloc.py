@@ -60,10 +60,16 @@ def test_noalloc_decode_matches_workspace_decode_twice():
 
 
 def test_noalloc_rejects_problems_larger_than_the_scratch():
-    q, k, v, kv_lens = _problem(3, 16, 64, 8, 16384, [16384] * 16)
-    need = engine.decode_workspace_bytes(q, k, v, is_causal=True, kv_lens=kv_lens)
+    # 16384 query rows x 16 splits of partials (136 MB): rejected before any
+    # launch, so K/V can be stride-0 views of one row instead of 137 GB.
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(3)
+    q = torch.randn(64, 256, 1, 128, generator=gen, device="cuda").to(torch.bfloat16)
+    k = torch.zeros(1, 1, 1, 128, dtype=torch.bfloat16, device="cuda").expand(64, 32, 131072, 128)
+    v = k
+    need = engine.decode_workspace_bytes(q, k, v, is_causal=True)
     assert need > _lib.NOALLOC_SCRATCH_BYTES
-    status, _, _ = _noalloc(q, k, v, kv_lens)
+    status, _, _ = _noalloc(q, k, v, None)
     assert status == _lib.ERR_WORKSPACE
     with pytest.raises(_lib.EngineError, match="8 MiB"):
-        engine.decode_noalloc(q, k, v, is_causal=True, kv_lens=kv_lens)
+        engine.decode_noalloc(q, k, v, is_causal=True)
