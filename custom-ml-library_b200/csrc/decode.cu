@@ -451,6 +451,34 @@ static cudaError_t decode_nq(const DecodeLaunch& L, cudaStream_t st) {
   return cudaErrorInvalidValue;
 }
 
+template <typename T, int D>
+static cudaError_t combine_only(const DecodeLaunch& L, cudaStream_t st) {
+  const int rows = L.p.batch * L.p.q_heads * L.p.q_len;
+  decode_combine_kernel<T, D><<<ceil_div(rows * 32, 256), 256, 0, st>>>(L);
+  return cudaGetLastError();
+}
+
+static cudaError_t decode_combine(const DecodeLaunch& L, cudaStream_t st) {
+  const int D = L.p.head_dim;
+  switch (L.p.dtype) {
+    case TS_F16:
+      if (D == 64) return combine_only<__half, 64>(L, st);
+      if (D == 128) return combine_only<__half, 128>(L, st);
+      if (D == 256) return combine_only<__half, 256>(L, st);
+      break;
+    case TS_BF16:
+      if (D == 64) return combine_only<__nv_bfloat16, 64>(L, st);
+      if (D == 128) return combine_only<__nv_bfloat16, 128>(L, st);
+      if (D == 256) return combine_only<__nv_bfloat16, 256>(L, st);
+      break;
+    case TS_F32:
+      if (D == 64) return combine_only<float, 64>(L, st);
+      if (D == 128) return combine_only<float, 128>(L, st);
+      break;
+  }
+  return cudaErrorInvalidValue;
+}
+
 cudaError_t decode_forward(const ts_attn_params& p, void* ws, size_t ws_bytes, uint32_t* fault,
                            cudaStream_t st) {
   DecodeLaunch L;
@@ -463,6 +491,12 @@ cudaError_t decode_forward(const ts_attn_params& p, void* ws, size_t ws_bytes, u
   L.ws_ml = L.ws_acc ? L.ws_acc + rows * L.max_splits * p.value_dim : nullptr;
   L.fault = fault;
   if (L.max_splits > 1 && ws_bytes < decode_workspace(p)) return cudaErrorInvalidValue;
+  // Several query rows per KV head (GQA groups, multi-token steps): the grouped kernel.
+  if ((p.q_heads / p.kv_heads) * p.q_len >= 2) {
+    const cudaError_t e = decode_group_forward(p, L.split_keys, L.max_splits, L.ws_acc, L.ws_ml, fault, st);
+    if (e != cudaSuccess || L.max_splits <= 1) return e;
+    return decode_combine(L, st);
+  }
   const int D = p.head_dim;
   switch (p.dtype) {
     case TS_F16:
