@@ -415,7 +415,9 @@ __global__ void decode_int8_combine(Int8Launch L) {
                                     (int64_t)t * p.lse_stride[2]] = ll > 0.f ? (mm + __log2f(ll)) * kLn2 : -INFINITY;
 }
 
-static int int8_pick_nq(int nq) { return nq <= 1 ? 1 : nq <= 2 ? 2 : 4; }
+// At most two query rows per CTA: as for the half-precision grouped decode,
+// more rows cost registers and occupancy than the shared K/V pass saves.
+static int int8_pick_nq(int nq) { return nq <= 1 ? 1 : 2; }
 
 bool decode_int8_supported(const ts_attn_params& p) {
   if (p.dtype != TS_F16 && p.dtype != TS_BF16 && p.dtype != TS_F32) return false;
@@ -466,7 +468,6 @@ static cudaError_t int8_nq(const Int8Launch& L, cudaStream_t st) {
   switch (int8_pick_nq((L.p.q_heads / L.p.kv_heads) * L.p.q_len)) {
     case 1: return launch_int8<T, D, 1>(L, st);
     case 2: return launch_int8<T, D, 2>(L, st);
-    case 4: return launch_int8<T, D, 4>(L, st);
   }
   return cudaErrorInvalidValue;
 }

@@ -151,9 +151,9 @@ def _expected(q, kd, vd, lens, tq):
 DECODE_CASES = [
     # (dtype, B, Hq, Hkv, D, per-row lengths, query tokens)
     ("float16", 2, 8, 8, 128, [700, 1500], 1),
-    ("bfloat16", 2, 16, 2, 128, [4100, 257], 1),  # 8 query heads per KV head: two groups of 4
+    ("bfloat16", 2, 16, 2, 128, [4100, 257], 1),  # 8 query heads per KV head: four groups of 2
     ("float32", 3, 4, 2, 64, [33, 2, 900], 2),
-    ("float16", 1, 6, 2, 256, [3000], 1),  # 3 rows per KV head: one group with a dead slot
+    ("float16", 1, 6, 2, 256, [3000], 1),  # 3 rows per KV head: the second group has a dead slot
     ("bfloat16", 3, 4, 4, 64, [0, 50, 31], 1),  # an empty row: zero output, lse -inf
     ("float16", 2, 4, 1, 128, [9000, 8191], 1),
 ]
