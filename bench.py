@@ -49,6 +49,8 @@ WORKLOADS = {
     "c4": dict(batch=64, heads=32, head_dim=128, min_len=1024, max_len=8192, decode_steps=256),
     # config 3 with the int8 KV cache (KVCache(quantized=True)): quantising append + fused-dequant decode
     "c4q": dict(batch=64, heads=32, head_dim=128, min_len=1024, max_len=8192, decode_steps=256),
+    # config 3 with grouped-query attention (4 query heads per KV head): the grouped decode kernel
+    "c4gqa": dict(batch=64, heads=32, kv_heads=8, head_dim=128, min_len=1024, max_len=8192, decode_steps=256),
     # reduced c4q (0.55 GB int8 cache, still larger than L2), for profiler captures only
     "c4q_small": dict(batch=8, heads=32, head_dim=128, min_len=1024, max_len=8192, decode_steps=16),
 }
@@ -615,22 +617,24 @@ def run_c4(args, quantized=False):
 
     cfg = WORKLOADS[args.workload]
     B, H, D, S = cfg["batch"], cfg["heads"], cfg["head_dim"], cfg["decode_steps"]
+    Hkv = cfg.get("kv_heads", H)
     cap = cfg["max_len"] + S
     dev = torch.device("cuda", 0)
     lens0 = np.random.default_rng(4).integers(cfg["min_len"], cfg["max_len"] + 1, B)
     gen = torch.Generator(device=dev)
     gen.manual_seed(4)
-    kc = torch.randn(B, H, cap, D, generator=gen, device=dev).to(torch.float16)
-    vc = torch.randn(B, H, cap, D, generator=gen, device=dev).to(torch.float16)
-    qn, kn, vn = (torch.randn(S, B, H, 1, D, generator=gen, device=dev).to(torch.float16) for _ in range(3))
+    kc = torch.randn(B, Hkv, cap, D, generator=gen, device=dev).to(torch.float16)
+    vc = torch.randn(B, Hkv, cap, D, generator=gen, device=dev).to(torch.float16)
+    qn = torch.randn(S, B, H, 1, D, generator=gen, device=dev).to(torch.float16)
+    kn, vn = (torch.randn(S, B, Hkv, 1, D, generator=gen, device=dev).to(torch.float16) for _ in range(2))
     out = torch.empty(S, B, H, 1, D, dtype=torch.float16, device=dev)
     start_lens = torch.tensor(lens0, dtype=torch.int32, device=dev)
     lens = [torch.empty_like(start_lens), torch.empty_like(start_lens)]
     if quantized:
         # Quantise the synthetic fp16 prefix once (the same kernel a prefill append runs).
-        k8 = torch.empty(B, H, cap, D, dtype=torch.int8, device=dev)
+        k8 = torch.empty(B, Hkv, cap, D, dtype=torch.int8, device=dev)
         v8 = torch.empty_like(k8)
-        ks = torch.ones(B, H, cap, dtype=torch.float32, device=dev)
+        ks = torch.ones(B, Hkv, cap, dtype=torch.float32, device=dev)
         vs = torch.ones_like(ks)
         engine.kv_append_int8(kc, vc, k8, v8, ks, vs, compute_dtype=torch.float16, position=0)
         del kc, vc
@@ -658,7 +662,7 @@ def run_c4(args, quantized=False):
     evs, step_ms, clocks = _timed(args, step, 2)
     dec = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
     row_bytes = D + 4 if quantized else 2 * D  # int8 row + fp32 scale, or fp16 row
-    kv_bytes = float(sum(2 * H * row_bytes * (lens0 + s + 1).sum() for s in range(S)))
+    kv_bytes = float(sum(2 * Hkv * row_bytes * (lens0 + s + 1).sum() for s in range(S)))
     peaks, src = load_peaks()
     gbs = kv_bytes / (dec / 1e3) / 1e9
     tokens = B * S / (dec / 1e3)
@@ -667,20 +671,21 @@ def run_c4(args, quantized=False):
         "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16", "data": "synthetic",
         "config": {"workload": (f"{args.workload}: fp16 decode over an int8 KV cache (fp32 scale per token/head) "
-                                if quantized else "c4: fp16 KV-cache decode ")
-                               + f"B={B} H={H} D={D}, lengths U[{cfg['min_len']},"
+                                if quantized else f"{args.workload}: fp16 KV-cache decode ")
+                               + f"B={B} H={H} KV heads={Hkv} D={D}, lengths U[{cfg['min_len']},"
                                f"{cfg['max_len']}] per row, {S} decode steps each appending one token",
-                   "l2": f"cache {2 * B * H * cap * (D + 4) / 1e9 if quantized else 4 * B * H * cap * D / 1e9:.1f} GB, "
+                   "l2": f"cache {2 * B * Hkv * cap * (D + 4) / 1e9 if quantized else 4 * B * Hkv * cap * D / 1e9:.1f} GB, "
                          "larger than L2"},
         "decode": {"tokens_per_s": tokens, "hbm_gbs": gbs, "ms_per_token_step": dec / S,
                    "frac_of_measured_hbm": gbs / peaks["hbm_gbs"], "frac_of_nominal_8000": gbs / 8000.0},
         "roofline": {"bound": "hbm",
                      "kernel": ("decode step (kv_append_int8 + decode_int8 + combine)" if quantized
+                                else "decode step (kv_append + decode_group + combine)" if Hkv != H
                                 else "decode step (kv_append + decode_split + combine)"),
                      "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"],
                      "peak_source": f"{src} hbm_gbs", "traffic": None,
-                     "algorithmic": ("sum_b 2*H*L_b*(D+4) bytes (int8 K+V rows and fp32 scales read) per step"
-                                     if quantized else "sum_b 2*H*L_b*D*2 bytes (K+V fp16 read) per step")},
+                     "algorithmic": ("sum_b 2*Hkv*L_b*(D+4) bytes (int8 K+V rows and fp32 scales read) per step"
+                                     if quantized else "sum_b 2*Hkv*L_b*D*2 bytes (K+V fp16 read once per KV head) per step")},
         "gpu_launches": S * (2 + (1 if splits else 0)) * args.steps,
         "clocks": clocks,
     }
@@ -689,6 +694,8 @@ def run_c4(args, quantized=False):
         per_pair, bpp = cpu_decode_sample(cfg5, 2)
         mean_len = float(lens0.mean())
         per_pair *= mean_len / cfg["max_len"]
+        # The reference broadcasts each KV head to its query heads (nn/attention.py:93-100),
+        # so its decode cost scales with the query heads.
         line["cpu_baseline"] = {"value": B / (per_pair * B * H), "unit": "tokens/s", "cores": cpu_cores(),
                                 "kind": "port", "sample": "oracle dense decode of 2 (b,h) pairs vs an fp16 cache "
                                 f"of {cfg['max_len']} keys, scaled to the mean length {mean_len:.0f}"}
@@ -713,7 +720,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if args.workload in ("c3", "c4", "c4q", "c4q_small"):
+        if args.workload in ("c3", "c4", "c4q", "c4q_small", "c4gqa"):
             if world > 1:
                 raise SystemExit("the c3 / c4 parity configs run on one GPU; c5 is the multi-GPU workload")
             result = (run_c3(args) if args.workload == "c3"

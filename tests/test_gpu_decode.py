@@ -21,6 +21,8 @@ CASES = [
     (2, 2, 2, 2, 1500, 64, [1500, 700]),        # two query tokens, causal inside the step
     (2, 4, 4, 1, 5000, 256, [4999, 3]),
     (1, 8, 1, 1, 2100, 128, [2100]),            # rep 8
+    (2, 6, 2, 1, 2600, 256, [2600, 100]),       # rep 3 at D=256: the second row group has a dead slot
+    (2, 4, 2, 3, 1800, 64, [1800, 40]),         # rep 2 x 3 tokens: three row groups, causal inside the step
 ]
 
 
