@@ -85,7 +85,7 @@ __device__ __forceinline__ void int8_row_range(const ts_attn_params& p, int b, i
 // only the keys it holds, with the warp's running max; P.V: p * v_scale times
 // the unpacked V row, packed f32x2 FMAs.
 template <typename T, int D, int NQ>
-__global__ void __launch_bounds__(kThreads) decode_int8_kernel(Int8Launch L) {
+__global__ void __launch_bounds__(kThreads, 4) decode_int8_kernel(Int8Launch L) {
   constexpr bool kIntQ = !std::is_same<T, float>::value;
   const ts_attn_params& p = L.p;
   constexpr int kVec = 16;                 // int8 elements per 16-byte vector
