@@ -194,6 +194,8 @@ int ts_attn_fwd_dropout(const ts_attn_params* p, const ts_dropout* d, void* stre
   if (st != TS_OK) return st;
   tsa::DropoutArgs args;
   if (!make_dropout(d, args)) return TS_ERR_INVALID_ARGUMENT;
+  if (d->p > 0.0 && tsa::tc_fwd_supported(*p))
+    return from_cuda(tsa::tc_forward(*p, fault_ptr(), as_stream(stream), &args));
   return from_cuda(tsa::simt_forward(*p, as_stream(stream), d->p > 0.0 ? &args : nullptr));
 }
 

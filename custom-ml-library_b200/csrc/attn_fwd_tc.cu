@@ -86,11 +86,12 @@ struct TcFwdArgs {
   ts_attn_params p;
   int n_q_tiles;
   uint32_t* fault;
+  DropoutArgs drop;  // used by the kDrop instantiation only
 };
 
 }  // namespace
 
-template <int D, bool kBF16>
+template <int D, bool kBF16, bool kDrop>
 __global__ void __launch_bounds__(384, 1)
     tc_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, TcFwdArgs args) {
@@ -306,6 +307,21 @@ __global__ void __launch_bounds__(384, 1)
       // so the special function unit stays below the tensor core's time.
       uint32_t pk[kHN / 2];
       uint64_t sum2[2] = {ptx::f2pack(0.f, 0.f), ptx::f2pack(0.f, 0.f)};
+      // Dropout (kDrop): keep bits of this half's 64 keys, from the counter-based
+      // generator the generic kernels use (dropout.cuh); P.V sees p * keep / (1 - p),
+      // the row sum l does not.
+      uint32_t keep[2] = {0xffffffffu, 0xffffffffu};
+      if constexpr (kDrop) {
+        const uint32_t bh = (uint32_t)(b * p.q_heads + h);
+        keep[0] = keep[1] = 0u;
+#pragma unroll
+        for (int j4 = 0; j4 < kHN / 4; ++j4)
+          keep[j4 >> 3] |= dropout_keep4(args.drop, bh, (uint32_t)qi, (uint32_t)(k0 / 4 + j4)) << (4 * (j4 & 7));
+      }
+      auto dropped = [&](float pv, int c) -> float {
+        if constexpr (kDrop) return (keep[c >> 5] >> (c & 31)) & 1u ? pv * args.drop.inv_keep_f : 0.f;
+        return pv;
+      };
       if (!need_mask) {
         const uint64_t sc2 = ptx::f2pack(qk_scale, qk_scale), ng2 = ptx::f2pack(-safe, -safe);
 #pragma unroll
@@ -322,6 +338,8 @@ __global__ void __launch_bounds__(384, 1)
           sum2[(c >> 1) & 1] = ptx::add2(sum2[(c >> 1) & 1], p2);
           float p0, p1;
           ptx::f2unpack(p2, p0, p1);
+          p0 = dropped(p0, c);
+          p1 = dropped(p1, c + 1);
           pk[c / 2] = kBF16 ? ptx::pack_bf16_rhu(p0, p1) : ptx::pack_f16(p0, p1);
         }
       } else {
@@ -333,6 +351,8 @@ __global__ void __launch_bounds__(384, 1)
           p0 = (key < kv_end && (int64_t)key <= lim) ? p0 : 0.f;
           p1 = (key + 1 < kv_end && (int64_t)key + 1 <= lim) ? p1 : 0.f;
           sum2[0] = ptx::add2(sum2[0], ptx::f2pack(p0, p1));
+          p0 = dropped(p0, c);
+          p1 = dropped(p1, c + 1);
           pk[c / 2] = kBF16 ? ptx::pack_bf16(p0, p1) : ptx::pack_f16(p0, p1);
         }
       }
@@ -465,7 +485,7 @@ bool tc_fwd_supported(const ts_attn_params& p) {
 template <int D, bool BF16>
 static cudaError_t launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                              const TcFwdArgs& a, cudaStream_t st) {
-  auto kern = tc_fwd_kernel<D, BF16>;
+  auto kern = a.drop.p > 0.f ? tc_fwd_kernel<D, BF16, true> : tc_fwd_kernel<D, BF16, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::kSmem);
   if (e != cudaSuccess) return e;
   dim3 grid(a.n_q_tiles, a.p.q_heads, a.p.batch);
@@ -473,7 +493,7 @@ static cudaError_t launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, const
   return cudaGetLastError();
 }
 
-cudaError_t tc_forward(const ts_attn_params& p, uint32_t* fault, cudaStream_t st) {
+cudaError_t tc_forward(const ts_attn_params& p, uint32_t* fault, cudaStream_t st, const DropoutArgs* drop) {
   CUtensorMap mq, mk, mv;
   if (!make_map(&mq, p.q, p.dtype, p.batch, p.q_heads, p.q_len, p.head_dim, 128) ||
       !make_map(&mk, p.k, p.dtype, p.batch, p.kv_heads, p.kv_len, p.head_dim, 128) ||
@@ -483,6 +503,7 @@ cudaError_t tc_forward(const ts_attn_params& p, uint32_t* fault, cudaStream_t st
   a.p = p;
   a.n_q_tiles = ceil_div(p.q_len, kBM);
   a.fault = fault;
+  a.drop = drop ? *drop : DropoutArgs{};
   const bool bf = p.dtype == TS_BF16;
   if (p.head_dim == 64) return bf ? launch_tc<64, true>(mq, mk, mv, a, st) : launch_tc<64, false>(mq, mk, mv, a, st);
   return bf ? launch_tc<128, true>(mq, mk, mv, a, st) : launch_tc<128, false>(mq, mk, mv, a, st);

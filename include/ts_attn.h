@@ -205,8 +205,9 @@ typedef struct ts_dropout {
   uint64_t offset; /* call counter; a forward and its backward pass the same value */
 } ts_dropout;
 
-/* ts_attn_fwd with dropout (generic CUDA-core kernels, every dtype / shape /
- * mask of ts_attn_fwd).  p = 0 is the plain forward on the same kernels. */
+/* ts_attn_fwd with dropout: the tcgen05 kernel where ts_attn_fwd would use it,
+ * the generic CUDA-core kernels otherwise (every dtype / shape / mask of
+ * ts_attn_fwd).  p = 0 is the plain forward on the generic kernels. */
 TS_ATTN_API int ts_attn_fwd_dropout(const ts_attn_params* params, const ts_dropout* dropout, void* stream);
 
 /* Workspace bytes ts_attn_bwd_dropout needs. */
