@@ -201,7 +201,10 @@ int ts_attn_fwd_dropout(const ts_attn_params* p, const ts_dropout* d, void* stre
 
 size_t ts_attn_bwd_dropout_workspace_size(const ts_attn_bwd_params* bp) {
   if (!bp || check_params(&bp->fwd) != TS_OK) return 0;
-  return tsa::simt_backward_workspace(*bp);
+  const size_t simt = tsa::simt_backward_workspace(*bp);
+  if (!tsa::tc_bwd_supported(*bp)) return simt;
+  const size_t tc = tsa::tc_bwd_workspace(*bp);
+  return tc > simt ? tc : simt;
 }
 
 int ts_attn_bwd_dropout(const ts_attn_bwd_params* bp, const ts_dropout* d, void* workspace, size_t workspace_bytes,
@@ -213,6 +216,10 @@ int ts_attn_bwd_dropout(const ts_attn_bwd_params* bp, const ts_dropout* d, void*
     return TS_ERR_INVALID_ARGUMENT;
   tsa::DropoutArgs args;
   if (!make_dropout(d, args)) return TS_ERR_INVALID_ARGUMENT;
+  if (d->p > 0.0 && tsa::tc_bwd_supported(*bp)) {
+    if (!workspace || workspace_bytes < tsa::tc_bwd_workspace(*bp)) return TS_ERR_WORKSPACE;
+    return from_cuda(tsa::tc_backward(*bp, workspace, workspace_bytes, fault_ptr(), as_stream(stream), &args));
+  }
   if (!workspace || workspace_bytes < tsa::simt_backward_workspace(*bp)) return TS_ERR_WORKSPACE;
   return from_cuda(tsa::simt_backward(*bp, workspace, as_stream(stream), d->p > 0.0 ? &args : nullptr));
 }

@@ -81,11 +81,12 @@ struct TcBwdArgs {
   float* dq_acc;     // [B, Hq, Tq, D]
   int n_k_tiles;
   uint32_t* fault;
+  DropoutArgs drop;  // used by the kDrop instantiation only
 };
 
 }  // namespace
 
-template <int D, bool kBF16>
+template <int D, bool kBF16, bool kDrop>
 __global__ void __launch_bounds__(384, 1)
     tc_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
@@ -287,6 +288,24 @@ __global__ void __launch_bounds__(384, 1)
             nl2[c / 2] = ptx::f2pack(a.x, a.y), nl2[c / 2 + 1] = ptx::f2pack(a.z, a.w);
             nd2[c / 2] = ptx::f2pack(d4.x, d4.y), nd2[c / 2 + 1] = ptx::f2pack(d4.z, d4.w);
           }
+          // Dropout (kDrop): keep bit of (this key, column 32*half + c) in bit c.  The
+          // generator gives the bits of 4 consecutive keys per call, so the 4 lanes
+          // of a key quad each draw one column of every 4 and swap nibbles.
+          uint32_t kb = 0xffffffffu;
+          if constexpr (kDrop) {
+            kb = 0u;
+            const uint32_t bh = (uint32_t)(b * p.q_heads + it_head(it));
+            const uint32_t j4 = (uint32_t)key >> 2;
+            const int quad = lane & ~3, sub = lane & 3;
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+              const uint32_t nib = dropout_keep4(args.drop, bh, (uint32_t)(q0 + 32 * half + 4 * g + sub), j4);
+#pragma unroll
+              for (int t = 0; t < 4; ++t)
+                kb |= ((__shfl_sync(0xffffffffu, nib, quad + t) >> sub) & 1u) << (4 * g + t);
+            }
+          }
+          const float dinv = kDrop ? args.drop.inv_keep_f : 1.f;
           // Columns below c_min are masked; warp-uniform fast path when none of this half is.
           const bool all_vis = __all_sync(0xffffffffu, c_min <= 32 * half);
           const uint64_t sl2x2 = ptx::f2pack(sl2, sl2), scx2 = ptx::f2pack(scale, scale);
@@ -304,8 +323,17 @@ __global__ void __launch_bounds__(384, 1)
               p1 = col + 1 >= c_min ? p1 : 0.f;
             }
             const uint64_t p2 = ptx::f2pack(p0, p1);
-            const uint64_t t2 =
-                ptx::add2(ptx::f2pack(__uint_as_float(rd[c]), __uint_as_float(rd[c + 1])), nd2[c / 2]);
+            uint64_t t2;
+            if constexpr (kDrop) {
+              // dV uses p * keep / (1 - p_drop); dS = p * (dP * keep / (1 - p_drop) - delta) * scale.
+              const float f0 = (kb >> c) & 1u ? dinv : 0.f, f1 = (kb >> (c + 1)) & 1u ? dinv : 0.f;
+              t2 = ptx::fma2(ptx::f2pack(__uint_as_float(rd[c]), __uint_as_float(rd[c + 1])), ptx::f2pack(f0, f1),
+                             nd2[c / 2]);
+              p0 *= f0;
+              p1 *= f1;
+            } else {
+              t2 = ptx::add2(ptx::f2pack(__uint_as_float(rd[c]), __uint_as_float(rd[c + 1])), nd2[c / 2]);
+            }
             const uint64_t ds2 = ptx::fma2(ptx::fma2(p2, scx2, 0ull), t2, 0ull);
             float d0, d1;
             ptx::f2unpack(ds2, d0, d1);
@@ -513,7 +541,7 @@ __global__ void bwd_stats_kernel(ts_attn_bwd_params bp, float* stats, int t_pad)
 template <int D, bool BF16>
 static cudaError_t launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                               const CUtensorMap& mdo, const TcBwdArgs& a, cudaStream_t st) {
-  auto kern = tc_bwd_kernel<D, BF16>;
+  auto kern = a.drop.p > 0.f ? tc_bwd_kernel<D, BF16, true> : tc_bwd_kernel<D, BF16, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdCfg<D>::kSmem);
   if (e != cudaSuccess) return e;
   dim3 grid(a.n_k_tiles, a.p.kv_heads, a.p.batch);
@@ -522,7 +550,7 @@ static cudaError_t launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, cons
 }
 
 cudaError_t tc_backward(const ts_attn_bwd_params& bp, void* ws, size_t ws_bytes, uint32_t* fault,
-                        cudaStream_t st) {
+                        cudaStream_t st, const DropoutArgs* drop) {
   const ts_attn_params& p = bp.fwd;
   if (ws_bytes < tc_bwd_workspace(bp)) return cudaErrorInvalidValue;
   const size_t rows = (size_t)p.batch * p.q_heads * p.q_len;
@@ -557,6 +585,7 @@ cudaError_t tc_backward(const ts_attn_bwd_params& bp, void* ws, size_t ws_bytes,
   a.dq_acc = dq_acc;
   a.n_k_tiles = ceil_div(p.kv_len, kBN);
   a.fault = fault;
+  a.drop = drop ? *drop : DropoutArgs{};
   const bool bf = p.dtype == TS_BF16;
   if (p.head_dim == 64)
     e = bf ? launch_bwd<64, true>(mq, mk, mv, mdo, a, st) : launch_bwd<64, false>(mq, mk, mv, mdo, a, st);

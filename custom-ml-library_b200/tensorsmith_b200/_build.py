@@ -15,6 +15,7 @@ import re
 import shutil
 import subprocess
 import sys
+import time
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -51,9 +52,13 @@ def _compile(src: Path, verbose_ptxas: bool) -> tuple[Path, str]:
     cmd = [nvcc(), *ARCH, *FLAGS, f"-I{INCLUDE}", "-c", str(src), "-o", str(obj)]
     if verbose_ptxas:
         cmd += ["-Xptxas", "-v"]
+    started = time.time()
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"nvcc failed for {src.name}:\n{res.stderr}")
+    # Stamp the object with the time its sources were read, so a source edited
+    # while nvcc ran is newer than the object and gets rebuilt next time.
+    os.utime(obj, (started, started))
     return obj, res.stderr
 
 
