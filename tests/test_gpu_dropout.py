@@ -120,3 +120,39 @@ def test_sdpa_dropout_api_and_tape():
     for backend in ("streaming", "native"):
         with pytest.raises(ValueError, match="dense backend"):
             nn.scaled_dot_product_attention(*tensors, dropout_p=0.1, backend=backend)
+
+
+TC_CASES = [
+    # (dtype, B, Hq, Hkv, Tq, Tk, D, causal, offset, p): shapes the tcgen05 kernels take,
+    # several key tiles, lengths that are not multiples of the tile or of a key quad
+    ("bfloat16", 1, 4, 2, 200, 331, 64, True, 131, 0.2),
+    ("bfloat16", 2, 2, 2, 130, 130, 128, False, 0, 0.5),
+    ("float16", 1, 2, 1, 257, 257, 128, True, 0, 0.1),
+]
+
+
+@pytest.mark.parametrize("case", TC_CASES, ids=lambda c: f"{c[0]}-D{c[6]}-T{c[4]}x{c[5]}-p{c[9]}")
+def test_tcgen05_dropout_matches_oracle(case):
+    """The tensor-core forward and backward (kDrop instantiations) draw the same
+    mask as the materialised one and match the oracle's dense dropout VJP."""
+    name, b, hq, hkv, tq, tk, d, causal, offset, p = case
+    rng = np.random.default_rng(tq + tk + d)
+    q, k, v = (rng.normal(size=s) for s in ((b, hq, tq, d), (b, hkv, tk, d), (b, hkv, tk, d)))
+    g = rng.normal(size=(b, hq, tq, d))
+    qr, kr, vr, gr = (rounded(x, name) for x in (q, k, v, g))
+    tq_, tk_, tv_, tg_ = (to_cuda(x, name) for x in (q, k, v, g))
+    args = (p, 4242, 7)
+    kw = dict(is_causal=causal, causal_offset=offset)
+    assert engine.fwd_path(tq_, tk_, tv_, **kw) == "tcgen05"
+    out, lse = engine.forward(tq_, tk_, tv_, dropout=args, **kw)
+    assert engine.bwd_path(tq_, tk_, tv_, out, lse, tg_, **kw) == "tcgen05"
+    dq, dk, dvv = engine.backward(tq_, tk_, tv_, out, lse, tg_, dropout=args, **kw)
+    torch.cuda.synchronize()
+    keep = engine.dropout_mask(b, hq, tq, tk, args, "cuda:0").cpu().numpy().astype(bool)
+    okw = dict(is_causal=causal, causal_offset=offset, enable_gqa=hq != hkv, dropout_keep=keep, dropout_p=p)
+    ref_o, ref_l = oracle.attention_forward(qr, kr, vr, algorithm="dense", **okw)
+    assert_close(to_np(out), ref_o, name, "tc dropout out")
+    assert_close(to_np(lse), ref_l, "float32", "tc dropout lse")
+    rdq, rdk, rdv = oracle.attention_backward_dense(qr, kr, vr, gr, None, **okw)
+    for got, ref, what in ((dq, rdq, "dq"), (dk, rdk, "dk"), (dvv, rdv, "dv")):
+        assert_close(to_np(got), ref, name, f"tc dropout {what}")
