@@ -286,11 +286,20 @@ def run_engine(args, rank: int, world: int, local_rank: int):
 
     splits = engine.decode_workspace_bytes(qd[0], kc[:, :, :cap], vc[:, :, :cap], is_causal=True,
                                            causal_offset=cap - 1) > 0
+    # With N > 1 each decode token's gather is queued on the process group's
+    # stream and waited for at the end of the step, so it overlaps the next
+    # token's append and decode.  (Splitting the prefill into blocks of pairs to
+    # overlap its gather costs more in per-block causal tails than it saves.)
     launches_per_step = 1 + S * (2 + (1 if splits else 0))
 
     def gather(src, dst):
         if world > 1:
             gather_to_root(src, plan, out=dst)
+
+    def gather_async(src, full):
+        # full: [world, ...] on rank 0; rank r's shard lands in full[r:r+1]
+        targets = None if full is None else [full[r : r + 1] for r in range(world)]
+        return gather_to_root(src, plan, out=targets, async_op=True)
 
     def step(ev):
         ev[0].record()
@@ -298,11 +307,15 @@ def run_engine(args, rank: int, world: int, local_rank: int):
         ev[1].record()
         gather(o, o_full)
         ev[2].record()
+        works = []
         for s in range(S):
             engine.kv_append(kd[s], vd[s], kc, vc, position=T + s)
             engine.decode(qd[s], kc[:, :, : T + s + 1], vc[:, :, : T + s + 1], is_causal=True,
                           causal_offset=T + s, out=od[s], workspace=ws)
-            gather(od[s], None if od_full is None else od_full[s])
+            if world > 1:
+                works.append(gather_async(od[s], None if od_full is None else od_full[s]))
+        for work in works:
+            work.wait()
         ev[3].record()
 
     def new_events():
@@ -374,7 +387,8 @@ def run_engine(args, rank: int, world: int, local_rank: int):
             "config": {
                 "workload": (f"{args.workload}: causal prefill bf16 B={B} H={H} D={D} T={T}, then {S} decode "
                              f"steps (KV append + split-K decode), (b,h) pairs sharded over {world} GPU(s), "
-                             "outputs gathered to rank 0 over NCCL"),
+                             "outputs gathered to rank 0 over NCCL (decode gathers queued and waited for at the "
+                             "end of the step)"),
                 "global_batch": B, "seq_len": T, "parallelism": f"bxh-shard{world}",
                 "l2": "inputs larger than L2 (Q/K/V/cache >= 8 GB per step)",
             },

@@ -80,36 +80,54 @@ def shard_view(x: torch.Tensor, plan: ShardPlan, group: int = 1) -> torch.Tensor
     return flat[:, plan.start * group : plan.stop * group]
 
 
-def gather_to_root(local: torch.Tensor, plan: ShardPlan, out: torch.Tensor | None = None,
-                   root: int = 0, group=None):
-    """Gather every rank's shard into ``out`` (the full tensor, same pair order) on ``root``.
+def gather_to_root(local: torch.Tensor, plan: ShardPlan, out=None, root: int = 0, group=None,
+                   async_op: bool = False):
+    """Gather every rank's shard into ``out`` on ``root``.
 
-    One NCCL gather (grouped send/recv) per call; other ranks return None.
-    Shards must be equal-sized (the plan is even)."""
+    ``out`` is the full tensor (the ranks' shards stacked along dim 0 in rank
+    order, contiguous) or a list of one contiguous tensor per rank shaped like
+    ``local``, which lets a caller gather one block of its pairs at a time into
+    strided places of a larger buffer.  One NCCL gather (grouped send/recv) per
+    call; other ranks return None.  Shards must be equal-sized (the plan is even).
+
+    With ``async_op=True`` the call returns the collective's work handle (None
+    on a single rank) instead of ``out``.  The gather runs on the process
+    group's stream after the work already queued on the current stream; the
+    current stream goes on without it (the next block's kernels overlap the
+    transfer) until ``work.wait()`` orders it after the gather."""
     if plan.world_size == 1:
-        if out is not None:
-            out.copy_(local)
-            return out
-        return local
+        target = out[0] if isinstance(out, (list, tuple)) else out
+        if target is not None:
+            target.copy_(local)
+        if async_op:
+            return None
+        return target if target is not None else local
     if not plan.even:
         raise ValueError("gather needs an even shard plan (pairs divisible by world size)")
     rank = dist.get_rank(group)
-    if rank == root:
-        if out is None:
-            shape = list(local.shape)
-            shape[0] *= plan.world_size
-            out = torch.empty(shape, dtype=local.dtype, device=local.device)
-        chunks = list(out.reshape((plan.world_size, -1) + tuple(local.shape[2:])).unbind(0)) \
-            if out.is_contiguous() else None
-        if chunks is None:
-            raise ValueError("gather target must be contiguous")
-        chunks = [c.view(local.shape) for c in chunks]
-        contiguous = all(c.is_contiguous() for c in chunks)
-        targets = chunks if contiguous else [torch.empty_like(local) for _ in chunks]
-        dist.gather(local.contiguous(), targets, dst=root, group=group)
-        if not contiguous:
-            for c, t in zip(chunks, targets):
-                c.copy_(t)
-        return out
-    dist.gather(local.contiguous(), None, dst=root, group=group)
-    return None
+    if rank != root:
+        work = dist.gather(local.contiguous(), None, dst=root, group=group, async_op=async_op)
+        return work if async_op else None
+    if isinstance(out, (list, tuple)):
+        if len(out) != plan.world_size or any(t.shape != local.shape or not t.is_contiguous() for t in out):
+            raise ValueError("gather targets must be one contiguous tensor per rank shaped like the shard")
+        work = dist.gather(local.contiguous(), list(out), dst=root, group=group, async_op=async_op)
+        return work if async_op else out
+    if out is None:
+        shape = list(local.shape)
+        shape[0] *= plan.world_size
+        out = torch.empty(shape, dtype=local.dtype, device=local.device)
+    if not out.is_contiguous():
+        raise ValueError("gather target must be contiguous")
+    chunks = [c.view(local.shape) for c in out.reshape((plan.world_size, -1) + tuple(local.shape[2:])).unbind(0)]
+    contiguous = all(c.is_contiguous() for c in chunks)
+    if async_op and not contiguous:
+        raise ValueError("an asynchronous gather needs targets that are contiguous per rank")
+    targets = chunks if contiguous else [torch.empty_like(local) for _ in chunks]
+    work = dist.gather(local.contiguous(), targets, dst=root, group=group, async_op=async_op)
+    if async_op:
+        return work
+    if not contiguous:
+        for c, t in zip(chunks, targets):
+            c.copy_(t)
+    return out

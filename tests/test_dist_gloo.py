@@ -58,8 +58,17 @@ def _worker(rank, world, port, queue):
         plan = ShardPlan(b, h, world, rank)
         local = shard_view(full, plan) * 1.0
         out = gather_to_root(local, plan)
+        # block by block, asynchronously, into per-rank strided places of one buffer
+        blocks = torch.zeros(world, plan.size, t, d) if rank == 0 else None
+        works = []
+        for c0 in range(0, plan.size, 2):
+            targets = [blocks[r : r + 1, c0 : c0 + 2] for r in range(world)] if rank == 0 else None
+            works.append(gather_to_root(local[:, c0 : c0 + 2], plan, out=targets, async_op=True))
+        for work in works:
+            work.wait()
         if rank == 0:
-            queue.put(("ok", torch.equal(out.reshape(b, h, t, d), full)))
+            queue.put(("ok", torch.equal(out.reshape(b, h, t, d), full)
+                       and torch.equal(blocks.reshape(b, h, t, d), full)))
         else:
             queue.put(("ok", out is None))
     except Exception as error:  # pragma: no cover - reported to the parent
