@@ -30,6 +30,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -43,8 +44,10 @@ WORKLOADS = {
     "c5": dict(batch=32, heads=32, head_dim=128, prefill=32768, decode_steps=128),
     # reduced shape of the same kernels, for profiler captures only
     "small": dict(batch=4, heads=32, head_dim=128, prefill=4096, decode_steps=4),
+    # the C5 prefill shape on 8 (b,h) pairs (forward + backward, 268 MB of inputs): profiler captures
+    "c5slice": dict(batch=1, heads=8, head_dim=128, prefill=32768, scale_inputs=False),
     # causal prefill bf16 forward + backward
-    "c3": dict(batch=8, heads=16, head_dim=128, prefill=4096),
+    "c3": dict(batch=8, heads=16, head_dim=128, prefill=4096, scale_inputs=True),
     # fp16 KV-cache decode, ragged lengths U[1024, 8192], 256 steps with append
     "c4": dict(batch=64, heads=32, head_dim=128, min_len=1024, max_len=8192, decode_steps=256),
     # config 3 with the int8 KV cache (KVCache(quantized=True)): quantising append + fused-dequant decode
@@ -70,6 +73,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
+    ap.add_argument("--clock-log", default=None,
+                    help="file for the nvidia-smi clock samples of the timed region (default: a temp file)")
     return ap.parse_args()
 
 
@@ -90,14 +95,56 @@ def load_peaks():
 
 
 # --------------------------------------------------------------------------
+# parity of the timed outputs: an fp64 restatement of attention on sampled
+# rows, run on the host after the timed region (not the oracle package)
+# --------------------------------------------------------------------------
+def ref_rows(q_rows, k, v, limits, scale):
+    """fp64 attention of query rows q_rows [R, D] against k [L, D] / v [L, C]; row r sees keys
+    [0, limits[r]).  Returns (out [R, C], lse [R])."""
+    import torch
+
+    s = (q_rows.double() @ k.double().T) * scale
+    keys = torch.arange(k.shape[0])
+    s = s.masked_fill(keys[None, :] >= torch.as_tensor(limits)[:, None], float("-inf"))
+    m = s.max(dim=1, keepdim=True).values
+    e = torch.exp(s - m)
+    l = e.sum(dim=1, keepdim=True)
+    return (e @ v.double()) / l, (m + torch.log(l))[:, 0]
+
+
+def ref_slice_backward(q, k, v, do, scale):
+    """fp64 causal attention of one (b, h) slice and its VJP: (o, lse, dq, dk, dv)."""
+    import torch
+
+    q, k, v, do = (x.double() for x in (q, k, v, do))
+    t = q.shape[0]
+    s = (q @ k.T) * scale
+    s = s.masked_fill(torch.ones(t, t, dtype=torch.bool).triu(1), float("-inf"))
+    lse = torch.logsumexp(s, dim=1)
+    p = torch.exp(s - lse[:, None])
+    o = p @ v
+    dv = p.T @ do
+    dp = do @ v.T
+    ds = p * (dp - (do * o).sum(dim=1, keepdim=True)) * scale
+    return o, lse, ds @ k, ds.T @ q, dv
+
+
+def max_abs(got, ref) -> float:
+    return float((got.double().cpu() - ref.double().cpu()).abs().max())
+
+
+# --------------------------------------------------------------------------
 # clocks sampled during the timed region
 # --------------------------------------------------------------------------
 class ClockSampler:
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, path=None):
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_gpu{gpu_index}.csv"
+        if path is None:
+            fd, path = tempfile.mkstemp(prefix=f"ts_clocks_gpu{gpu_index}_", suffix=".csv")
+            os.close(fd)
+        self.path = Path(path)
         try:
-            self.path.parent.mkdir(exist_ok=True)
+            self.path.parent.mkdir(parents=True, exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits",
@@ -245,6 +292,29 @@ def run_reference(args, rank: int, world: int):
 # --------------------------------------------------------------------------
 # engine arm
 # --------------------------------------------------------------------------
+def parity_c5(q, kc, vc, o, qd, od, T, S, D, seed=7):
+    """Sampled check of the timed step's outputs on this rank: the first and last (b,h) pair,
+    the last 128 prefill rows plus 128 random ones, and decode steps 0 and S-1."""
+    import torch
+
+    gen = torch.Generator().manual_seed(seed)
+    n = q.shape[1]
+    rows = torch.cat([torch.arange(T - 128, T), torch.randperm(T - 128, generator=gen)[:128].sort().values])
+    scale = D ** -0.5
+    err_o = err_d = 0.0
+    for pr in sorted({0, n - 1}):
+        kh, vh = kc[0, pr, : T + S].cpu(), vc[0, pr, : T + S].cpu()
+        ref, _ = ref_rows(q[0, pr].cpu()[rows], kh[:T], vh[:T], rows + 1, scale)
+        err_o = max(err_o, max_abs(o[0, pr].cpu()[rows], ref))
+        for st in sorted({0, S - 1}):
+            ref_d, _ = ref_rows(qd[st, 0, pr].cpu(), kh, vh, [T + st + 1], scale)
+            err_d = max(err_d, max_abs(od[st, 0, pr].cpu(), ref_d))
+    return {"max_abs_prefill_out": err_o, "max_abs_decode_out": err_d, "tolerance_max_abs": 2e-2,
+            "pass": max(err_o, err_d) <= 2e-2,
+            "rows": f"(b,h) pairs {sorted({0, n - 1})} of rank 0: last 128 + 128 random prefill rows, "
+                    f"decode steps {sorted({0, S - 1})}; fp64 reference on the host"}
+
+
 def run_engine(args, rank: int, world: int, local_rank: int):
     import numpy as np
     import torch
@@ -331,7 +401,7 @@ def run_engine(args, rank: int, world: int, local_rank: int):
         step(new_events())
     barrier()
     engine.check_device_status(dev)
-    sampler = ClockSampler(local_rank) if rank == 0 else None
+    sampler = ClockSampler(local_rank, args.clock_log) if rank == 0 else None
     barrier()
     evs = [new_events() for _ in range(args.steps)]
     t_start = torch.cuda.Event(enable_timing=True)
@@ -409,6 +479,7 @@ def run_engine(args, rank: int, world: int, local_rank: int):
         }
         if e2e is not None:
             result["e2e"] = e2e
+        result["parity"] = parity_c5(q, kc, vc, o, qd, od, T, S, D)
         if world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
     return result
@@ -491,26 +562,30 @@ def run_e2e(args, cfg, plan, rank, world, local_rank, q, kc, vc, qd, kd, vd, ws,
                              non_blocking=True)
         compute.wait_event(s_out.record_event())
 
-    steps = max(1, min(args.steps, 2))
+    steps = max(1, args.steps)
     step()
     barrier()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for _ in range(steps):
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    evs[0].record()
+    for i in range(steps):
         step()
-    ev1.record()
+        evs[i + 1].record()
     barrier()
     import torch.distributed as dist
 
-    ms = torch.tensor([ev0.elapsed_time(ev1) / steps], device=dev, dtype=torch.float64)
+    per_step = [evs[i].elapsed_time(evs[i + 1]) for i in range(steps)]
+    stats = torch.tensor([evs[0].elapsed_time(evs[-1]) / steps, min(per_step), max(per_step)], device=dev,
+                         dtype=torch.float64)
     if world > 1:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = ms.item()
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    ms, ms_min, ms_max = stats.tolist()
     flops = causal_flops(B * H, T, T, 0, D)
     esz = q.element_size()
     h2d = (3 * n * T * D + 3 * S * n * D) * esz
     d2h = (world * n * T * D + S * world * n * D) * esz if rank == 0 else 0
     return {"value": flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+            "ms_per_step_min": ms_min, "ms_per_step_max": ms_max,
+            "value_min": flops / (ms_max / 1e3) / 1e12, "value_max": flops / (ms_min / 1e3) / 1e12,
             "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h, "steps": steps,
             "path": "tensorsmith_b200.engine (C ABI) with pinned host inputs/outputs; prefill inputs "
                     f"copied in {n_chunks} (b,h) chunks on a copy stream overlapping the forward of the "
@@ -527,7 +602,7 @@ def _timed(args, step, n_events):
         step([torch.cuda.Event(enable_timing=True) for _ in range(n_events)])
     torch.cuda.synchronize()
     engine.check_device_status()
-    sampler = ClockSampler(torch.cuda.current_device())
+    sampler = ClockSampler(torch.cuda.current_device(), args.clock_log)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_events)] for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
@@ -541,18 +616,20 @@ def _timed(args, step, n_events):
 
 
 def run_c3(args):
-    """Causal prefill bf16 B=8 H=16 T=4096 D=128: forward + backward."""
+    """Causal prefill bf16 forward + backward: B=8 H=16 T=4096 D=128 (Q/K/V scaled
+    by 1/sqrt(D)), or the C5 prefill shape on 8 (b,h) pairs (``c5slice``, unscaled N(0,1) inputs)."""
     import numpy as np
     import torch
 
     from tensorsmith_b200 import engine
 
-    cfg = WORKLOADS["c3"]
+    cfg = WORKLOADS[args.workload]
     B, H, T, D = cfg["batch"], cfg["heads"], cfg["prefill"], cfg["head_dim"]
+    in_scale = D ** -0.5 if cfg.get("scale_inputs") else 1.0
     dev = torch.device("cuda", 0)
     gen = torch.Generator(device=dev)
     gen.manual_seed(2)
-    q, k, v = ((torch.randn(B, H, T, D, generator=gen, device=dev) / D ** 0.5).to(torch.bfloat16) for _ in range(3))
+    q, k, v = ((torch.randn(B, H, T, D, generator=gen, device=dev) * in_scale).to(torch.bfloat16) for _ in range(3))
     do = torch.randn(B, H, T, D, generator=gen, device=dev).to(torch.bfloat16)
     out = torch.empty_like(q)
     lse = torch.empty(B, H, T, dtype=torch.float32, device=dev)
@@ -573,13 +650,35 @@ def run_c3(args):
     value = 14.0 * pairs_flops / ((fwd + bwd) / 1e3) / 1e12
     bwd_tf = 10.0 * pairs_flops / (bwd / 1e3) / 1e12
     fwd_tf = 4.0 * pairs_flops / (fwd / 1e3) / 1e12
+    # parity of the last timed step, fp64 on the host: one (b,h) slice in full (forward and
+    # gradients), or at T = 32768 the forward on 256 sampled rows of it
+    bs, hs = B - 1, H - 1
+    if T <= 8192:
+        ro, rl, rdq, rdk, rdv = ref_slice_backward(q[bs, hs].cpu(), k[bs, hs].cpu(), v[bs, hs].cpu(),
+                                                   do[bs, hs].cpu(), D ** -0.5)
+        errs = {"out": max_abs(out[bs, hs], ro), "lse": max_abs(lse[bs, hs], rl), "dq": max_abs(dq[bs, hs], rdq),
+                "dk": max_abs(dk[bs, hs], rdk), "dv": max_abs(dv[bs, hs], rdv)}
+        peaks_ref = {"dq": float(rdq.abs().max()), "dk": float(rdk.abs().max()), "dv": float(rdv.abs().max())}
+        rows_note = f"(b,h) = ({bs},{hs}) in full"
+    else:
+        rows = torch.cat([torch.arange(T - 128, T), torch.randperm(T - 128, generator=torch.Generator().manual_seed(7))[:128].sort().values])
+        ro, rl = ref_rows(q[bs, hs].cpu()[rows], k[bs, hs].cpu(), v[bs, hs].cpu(), rows + 1, D ** -0.5)
+        errs = {"out": max_abs(out[bs, hs].cpu()[rows], ro), "lse": max_abs(lse[bs, hs].cpu()[rows], rl)}
+        peaks_ref = {}
+        rows_note = f"(b,h) = ({bs},{hs}): forward on the last 128 + 128 random rows"
+    parity = {"max_abs": errs, "max_abs_ref_grad": peaks_ref, "tolerance_max_abs": 2e-2,
+              "pass": max(errs["out"], errs["lse"]) <= 2e-2
+              and all(errs[g] <= 2e-2 * max(1.0, peaks_ref[g]) for g in peaks_ref),
+              "rows": rows_note + "; fp64 reference on the host; gradients held to 2e-2 * max(1, max|ref|)"}
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"c3: causal attention bf16 B={B} H={H} T={T} D={D}, forward + backward, "
-                               "Q/K/V ~ N(0,1)/sqrt(128), dO ~ N(0,1)",
-                   "l2": "inputs larger than L2 (0.7 GB per step)"},
+        "config": {"workload": f"{args.workload}: causal attention bf16 B={B} H={H} T={T} D={D}, forward + "
+                               "backward, Q/K/V ~ N(0,1)" + ("/sqrt(128)" if in_scale != 1.0 else "")
+                               + ", dO ~ N(0,1)",
+                   "l2": f"inputs larger than L2 ({5 * B * H * T * D * 2 / 1e9:.2f} GB per step)"},
+        "parity": parity,
         "forward": {"tflops": fwd_tf, "ms": fwd, "frac_of_measured_bf16": fwd_tf / peaks["bf16_tflops"]},
         "backward": {"tflops": bwd_tf, "ms": bwd, "frac_of_measured_bf16": bwd_tf / peaks["bf16_tflops"],
                      "launches": "row-statistics preprocess + dQ accumulator memset + tc_bwd_kernel + dQ convert"},
@@ -590,7 +689,7 @@ def run_c3(args):
         "gpu_launches": 4 * args.steps,  # tc_fwd_kernel, bwd_stats_kernel, tc_bwd_kernel, dq_convert_kernel
         "clocks": clocks,
     }
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and args.workload == "c3":
         line["cpu_baseline"] = cpu_c3_baseline(cfg, args.cpu_seconds)
     return line
 
@@ -675,6 +774,22 @@ def run_c4(args, quantized=False):
 
     evs, step_ms, clocks = _timed(args, step, 2)
     dec = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    # parity of the last decode step of the last timed step (4 sampled (b, h) rows, fp64 on the host)
+    prng = np.random.default_rng(5)
+    sample = [(B - 1, H - 1)] + [(int(prng.integers(B)), int(prng.integers(H))) for _ in range(3)]
+    err = 0.0
+    for b, h in sample:
+        hk, n = h // (H // Hkv), int(lens0[b]) + S
+        if quantized:
+            kh = kc[b, hk, :n].cpu().double() * ks[b, hk, :n].cpu().double()[:, None]
+            vh = vc[b, hk, :n].cpu().double() * vs[b, hk, :n].cpu().double()[:, None]
+        else:
+            kh, vh = kc[b, hk, :n].cpu(), vc[b, hk, :n].cpu()
+        ref, _ = ref_rows(qn[S - 1, b, h].cpu(), kh, vh, [n], D ** -0.5)
+        err = max(err, max_abs(out[S - 1, b, h], ref))
+    parity = {"max_abs_out": err, "tolerance_max_abs": 2e-2, "pass": err <= 2e-2,
+              "rows": f"last decode step, (b,h) = {sample}, dequantised cache" if quantized
+              else f"last decode step, (b,h) = {sample}"}
     row_bytes = D + 4 if quantized else 2 * D  # int8 row + fp32 scale, or fp16 row
     kv_bytes = float(sum(2 * Hkv * row_bytes * (lens0 + s + 1).sum() for s in range(S)))
     peaks, src = load_peaks()
@@ -690,6 +805,7 @@ def run_c4(args, quantized=False):
                                f"{cfg['max_len']}] per row, {S} decode steps each appending one token",
                    "l2": f"cache {2 * B * Hkv * cap * (D + 4) / 1e9 if quantized else 4 * B * Hkv * cap * D / 1e9:.1f} GB, "
                          "larger than L2"},
+        "parity": parity,
         "decode": {"tokens_per_s": tokens, "hbm_gbs": gbs, "ms_per_token_step": dec / S,
                    "frac_of_measured_hbm": gbs / peaks["hbm_gbs"], "frac_of_nominal_8000": gbs / 8000.0},
         "roofline": {"bound": "hbm",
@@ -734,14 +850,18 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if args.workload in ("c3", "c4", "c4q", "c4q_small", "c4gqa"):
+        from tensorsmith_b200 import _lib
+
+        build = {"lib": str(_lib.LIB_PATH.relative_to(ROOT)), "source_digest": _lib.library_digest()}
+        if args.workload in ("c3", "c5slice", "c4", "c4q", "c4q_small", "c4gqa"):
             if world > 1:
                 raise SystemExit("the c3 / c4 parity configs run on one GPU; c5 is the multi-GPU workload")
-            result = (run_c3(args) if args.workload == "c3"
+            result = (run_c3(args) if args.workload in ("c3", "c5slice")
                       else run_c4(args, quantized=args.workload.startswith("c4q")))
         else:
             result = run_engine(args, rank, world, local_rank)
         if rank == 0 and result is not None:
+            result["build"] = build
             print(json.dumps(result), flush=True)
     finally:
         if world > 1:

@@ -1,6 +1,7 @@
 // extern "C" entry points of libts_attn.so (declared in include/ts_attn.h):
 // argument validation, kernel selection and the device fault word.
 #include <cstdio>
+#include <mutex>
 
 #include "common.cuh"
 #include "decode.cuh"
@@ -8,6 +9,7 @@
 #include "kv_cache.cuh"
 #include "rope.cuh"
 #include "simt.cuh"
+#include "symbols.cuh"
 #include "tc_bwd.cuh"
 #include "tc_fwd.cuh"
 
@@ -16,17 +18,7 @@ namespace {
 // Fault word written by kernels whose bounded waits gave up (per device).
 __device__ uint32_t g_fault_word;
 
-uint32_t* fault_ptr() {
-  static uint32_t* ptrs[64] = {nullptr};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (!ptrs[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_fault_word) != cudaSuccess) return nullptr;
-    ptrs[dev] = static_cast<uint32_t*>(p);
-  }
-  return ptrs[dev];
-}
+uint32_t* fault_ptr() { return static_cast<uint32_t*>(tsa::device_symbol_address(&g_fault_word)); }
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
@@ -56,9 +48,53 @@ int check_params(const ts_attn_params* p) {
 
 }  // namespace
 
+namespace tsa {
+
+void* device_symbol_address(const void* symbol) {
+  // CUresult cuCtxGetId(CUcontext ctx, unsigned long long* id); ctx = NULL: the current context.
+  typedef int (*CtxGetIdFn)(void*, unsigned long long*);
+  struct Entry {
+    const void* symbol;
+    unsigned long long ctx;
+    void* ptr;
+  };
+  constexpr int kEntries = 256;
+  static Entry cache[kEntries];
+  static int used = 0;
+  static CtxGetIdFn ctx_get_id = nullptr;
+  static std::once_flag once;
+  static std::mutex lock;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      ctx_get_id = reinterpret_cast<CtxGetIdFn>(fn);
+  });
+  std::lock_guard<std::mutex> guard(lock);
+  unsigned long long ctx = 0;
+  bool have_ctx = ctx_get_id && ctx_get_id(nullptr, &ctx) == 0;
+  if (have_ctx)
+    for (int i = 0; i < used; ++i)
+      if (cache[i].symbol == symbol && cache[i].ctx == ctx) return cache[i].ptr;
+  void* ptr = nullptr;
+  if (cudaGetSymbolAddress(&ptr, symbol) != cudaSuccess || ptr == nullptr) return nullptr;
+  // The lookup above makes the device's primary context current if nothing was.
+  if (!have_ctx) have_ctx = ctx_get_id && ctx_get_id(nullptr, &ctx) == 0;
+  if (have_ctx && used < kEntries) cache[used++] = Entry{symbol, ctx, ptr};
+  return ptr;
+}
+
+}  // namespace tsa
+
 extern "C" {
 
 int ts_attn_abi_version(void) { return TS_ATTN_ABI_VERSION; }
+
+#ifndef TS_SOURCE_DIGEST
+#define TS_SOURCE_DIGEST "unknown"
+#endif
+const char* ts_attn_source_digest(void) { return TS_SOURCE_DIGEST; }
 
 const char* ts_attn_strerror(int status) {
   switch (status) {
@@ -96,7 +132,10 @@ size_t ts_attn_decode_workspace_size(const ts_attn_params* p) {
 int ts_attn_decode(const ts_attn_params* p, void* workspace, size_t workspace_bytes, void* stream) {
   const int st = check_params(p);
   if (st != TS_OK) return st;
-  if (!tsa::decode_supported(*p)) return from_cuda(tsa::simt_forward(*p, as_stream(stream)));
+  // Problems the split-K kernels do not take (many query rows, explicit masks,
+  // value_dim != head_dim) go where ts_attn_fwd would send them; neither path
+  // needs a workspace.
+  if (!tsa::decode_supported(*p)) return ts_attn_fwd(p, stream);
   const size_t need = tsa::decode_workspace(*p);
   if (need && (!workspace || workspace_bytes < need)) return TS_ERR_WORKSPACE;
   return from_cuda(tsa::decode_forward(*p, workspace, workspace_bytes, fault_ptr(), as_stream(stream)));
@@ -194,9 +233,9 @@ int ts_attn_fwd_dropout(const ts_attn_params* p, const ts_dropout* d, void* stre
   if (st != TS_OK) return st;
   tsa::DropoutArgs args;
   if (!make_dropout(d, args)) return TS_ERR_INVALID_ARGUMENT;
-  if (d->p > 0.0 && tsa::tc_fwd_supported(*p))
-    return from_cuda(tsa::tc_forward(*p, fault_ptr(), as_stream(stream), &args));
-  return from_cuda(tsa::simt_forward(*p, as_stream(stream), d->p > 0.0 ? &args : nullptr));
+  if (d->p == 0.0) return ts_attn_fwd(p, stream);  // no dropout: the plain path selection
+  if (tsa::tc_fwd_supported(*p)) return from_cuda(tsa::tc_forward(*p, fault_ptr(), as_stream(stream), &args));
+  return from_cuda(tsa::simt_forward(*p, as_stream(stream), &args));
 }
 
 size_t ts_attn_bwd_dropout_workspace_size(const ts_attn_bwd_params* bp) {
@@ -216,12 +255,13 @@ int ts_attn_bwd_dropout(const ts_attn_bwd_params* bp, const ts_dropout* d, void*
     return TS_ERR_INVALID_ARGUMENT;
   tsa::DropoutArgs args;
   if (!make_dropout(d, args)) return TS_ERR_INVALID_ARGUMENT;
-  if (d->p > 0.0 && tsa::tc_bwd_supported(*bp)) {
+  if (d->p == 0.0) return ts_attn_bwd(bp, workspace, workspace_bytes, stream);  // the plain path selection
+  if (tsa::tc_bwd_supported(*bp)) {
     if (!workspace || workspace_bytes < tsa::tc_bwd_workspace(*bp)) return TS_ERR_WORKSPACE;
     return from_cuda(tsa::tc_backward(*bp, workspace, workspace_bytes, fault_ptr(), as_stream(stream), &args));
   }
   if (!workspace || workspace_bytes < tsa::simt_backward_workspace(*bp)) return TS_ERR_WORKSPACE;
-  return from_cuda(tsa::simt_backward(*bp, workspace, as_stream(stream), d->p > 0.0 ? &args : nullptr));
+  return from_cuda(tsa::simt_backward(*bp, workspace, as_stream(stream), &args));
 }
 
 int ts_attn_dropout_mask(const ts_dropout* d, int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,

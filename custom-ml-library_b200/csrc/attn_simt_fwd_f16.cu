@@ -1,0 +1,10 @@
+// Generic CUDA-core attention forward, __half instantiations (simt_kernels.cuh).
+#include "simt_kernels.cuh"
+
+namespace tsa {
+
+cudaError_t simt_forward_f16(const ts_attn_params& p, cudaStream_t st, const DropoutArgs* drop) {
+  return simt_fwd_t<__half>(p, drop, st);
+}
+
+}  // namespace tsa

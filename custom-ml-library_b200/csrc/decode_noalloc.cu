@@ -13,17 +13,17 @@
 // held until the process exits.  Host code cannot use the array's name as a
 // device address (on the host it names a stand-in object), so the first call
 // on each device looks the real address up with cudaGetSymbolAddress while
-// that device is current and caches it; make that first call before any
-// stream capture.  Every call on a device shares the array, so calls that
+// that device is current and caches it under the context's unique id (a
+// context recreated after cudaDeviceReset looks it up again); make that first
+// call before any stream capture.  Every call on a device shares the array, so calls that
 // overlap on the GPU (different streams, or threads, without ordering) race on
 // it.  No byte of it has to start at zero: a call writes each partial before
 // it reads it, so the contents left by the previous call are never used.
 // Problems whose partials need more than the scratch size are rejected with
 // TS_ERR_WORKSPACE before anything is launched.  No cudaMalloc, cudaFree or
 // allocating library routine is called here.
-#include <mutex>
-
 #include "common.cuh"
+#include "symbols.cuh"
 
 namespace {
 
@@ -31,23 +31,6 @@ constexpr size_t kNoAllocScratchBytes = TS_ATTN_NOALLOC_SCRATCH_BYTES;
 static_assert(kNoAllocScratchBytes == (size_t)8 << 20, "scratch size is part of the ABI contract");
 
 static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
-
-// Device address of g_decode_scratch on the current device (looked up once per device).
-void* scratch_address() {
-  constexpr int kMaxDevices = 64;
-  static void* addr[kMaxDevices] = {nullptr};
-  static std::mutex lock;
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-  std::lock_guard<std::mutex> guard(lock);
-  if (!addr[dev]) {
-    void* ptr = nullptr;
-    const cudaError_t err = cudaGetSymbolAddress(&ptr, g_decode_scratch);
-    if (err != cudaSuccess || ptr == nullptr) return nullptr;
-    addr[dev] = ptr;
-  }
-  return addr[dev];
-}
 
 }  // namespace
 
@@ -57,7 +40,7 @@ extern "C" int ts_attn_decode_noalloc(const ts_attn_params* params, void* stream
   if (path != TS_PATH_DECODE) return ts_attn_decode(params, nullptr, 0, stream);  // needs no scratch
   const size_t need = ts_attn_decode_workspace_size(params);
   if (need > kNoAllocScratchBytes) return TS_ERR_WORKSPACE;
-  void* scratch = scratch_address();
+  void* scratch = tsa::device_symbol_address(&g_decode_scratch);
   if (scratch == nullptr) return TS_ERR_LAUNCH;
   return ts_attn_decode(params, scratch, kNoAllocScratchBytes, stream);
 }

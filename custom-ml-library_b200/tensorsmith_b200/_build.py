@@ -47,9 +47,23 @@ def nvcc() -> str:
     return found
 
 
+def _source_digest() -> str:
+    from ._lib import source_digest
+
+    return source_digest()
+
+
+DIGEST_STAMP = BUILD / "abi.digest"
+
+
 def _compile(src: Path, verbose_ptxas: bool) -> tuple[Path, str]:
     obj = BUILD / (src.stem + ".o")
     cmd = [nvcc(), *ARCH, *FLAGS, f"-I{INCLUDE}", "-c", str(src), "-o", str(obj)]
+    digest = None
+    if src.name == "abi.cu":
+        # The library reports the digest of the sources it was built from (ts_attn_source_digest).
+        digest = _source_digest()
+        cmd.append(f'-DTS_SOURCE_DIGEST="{digest}"')
     if verbose_ptxas:
         cmd += ["-Xptxas", "-v"]
     started = time.time()
@@ -59,6 +73,8 @@ def _compile(src: Path, verbose_ptxas: bool) -> tuple[Path, str]:
     # Stamp the object with the time its sources were read, so a source edited
     # while nvcc ran is newer than the object and gets rebuilt next time.
     os.utime(obj, (started, started))
+    if digest is not None:
+        DIGEST_STAMP.write_text(digest)
     return obj, res.stderr
 
 
@@ -66,12 +82,23 @@ def sources() -> list[Path]:
     return sorted(CSRC.glob("*.cu"))
 
 
+def _library_digest() -> str | None:
+    """Digest compiled into the library on disk (read in a child process, so this process never
+    maps a library it may be about to replace)."""
+    code = ("import ctypes,sys; f=ctypes.CDLL(sys.argv[1]).ts_attn_source_digest; "
+            "f.restype=ctypes.c_char_p; print(f().decode())")
+    res = subprocess.run([sys.executable, "-c", code, str(LIB)], capture_output=True, text=True)
+    return res.stdout.strip() if res.returncode == 0 else None
+
+
 def stale() -> bool:
     if not LIB.exists():
         return True
     built = LIB.stat().st_mtime
     deps = list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
-    return any(p.stat().st_mtime > built for p in deps)
+    if any(p.stat().st_mtime > built for p in deps):
+        return True
+    return _library_digest() != _source_digest()
 
 
 _INCLUDE_RE = re.compile(r'^\s*#\s*include\s*"([^"]+)"', re.M)
@@ -98,6 +125,8 @@ def _object_stale(src: Path) -> bool:
     """An object is rebuilt when its source or a header it includes (transitively) is newer."""
     obj = BUILD / (src.stem + ".o")
     if not obj.exists():
+        return True
+    if src.name == "abi.cu" and (not DIGEST_STAMP.exists() or DIGEST_STAMP.read_text() != _source_digest()):
         return True
     built = obj.stat().st_mtime
     return any(p.stat().st_mtime > built for p in _local_deps(src.resolve()))

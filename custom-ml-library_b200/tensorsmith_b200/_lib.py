@@ -8,11 +8,29 @@ missing or was built for another ABI, :func:`lib` raises.
 from __future__ import annotations
 
 import ctypes
+import hashlib
 import os
 from pathlib import Path
 
 ABI_VERSION = 1
 LIB_PATH = Path(__file__).resolve().parent / "lib" / "libts_attn.so"
+CSRC = Path(__file__).resolve().parent.parent / "csrc"
+INCLUDE = Path(__file__).resolve().parent.parent.parent / "include"
+
+
+def source_files() -> list[Path]:
+    """The files the library is compiled from, in file-name order."""
+    files = list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
+    return sorted(files, key=lambda f: f.name)
+
+
+def source_digest() -> str:
+    """SHA-256 of the sources (name, NUL, contents, NUL per file) -- what ts_attn_source_digest returns
+    for a library built from this tree."""
+    h = hashlib.sha256()
+    for f in source_files():
+        h.update(f.name.encode() + b"\0" + f.read_bytes() + b"\0")
+    return h.hexdigest()
 
 # ts_dtype
 F32, F16, BF16, F64 = 0, 1, 2, 3
@@ -152,6 +170,7 @@ SIGNATURES = {
          ctypes.c_size_t, ctypes.c_void_p],
     ),
     "ts_attn_device_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
+    "ts_attn_source_digest": (ctypes.c_char_p, []),
 }
 
 
@@ -185,8 +204,19 @@ def lib() -> ctypes.CDLL:
     version = handle.ts_attn_abi_version()
     if version != ABI_VERSION:
         raise RuntimeError(f"{path} has ABI version {version}, expected {ABI_VERSION}")
+    built_from = handle.ts_attn_source_digest().decode()
+    if "TS_ATTN_LIB" not in os.environ and CSRC.is_dir() and built_from != source_digest():
+        raise RuntimeError(
+            f"{path} was built from other sources (digest {built_from[:12]}, tree {source_digest()[:12]}); "
+            "rebuild it with `python -m tensorsmith_b200._build`"
+        )
     _LIB = handle
     return handle
+
+
+def library_digest() -> str:
+    """Source digest compiled into the loaded library."""
+    return lib().ts_attn_source_digest().decode()
 
 
 def strerror(status: int) -> str:

@@ -94,7 +94,12 @@ def gather_to_root(local: torch.Tensor, plan: ShardPlan, out=None, root: int = 0
     on a single rank) instead of ``out``.  The gather runs on the process
     group's stream after the work already queued on the current stream; the
     current stream goes on without it (the next block's kernels overlap the
-    transfer) until ``work.wait()`` orders it after the gather."""
+    transfer) until ``work.wait()`` orders it after the gather.  Because only
+    the handle comes back, an asynchronous call on ``root`` must be given
+    ``out`` (a ValueError otherwise): a buffer allocated here could not reach
+    the caller."""
+    if async_op and out is None and (plan.world_size == 1 or dist.get_rank(group) == root):
+        raise ValueError("an asynchronous gather needs `out` on the root rank (only the work handle is returned)")
     if plan.world_size == 1:
         target = out[0] if isinstance(out, (list, tuple)) else out
         if target is not None:

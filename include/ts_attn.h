@@ -123,6 +123,12 @@ TS_ATTN_API int ts_attn_abi_version(void);
 /* Static description of a status code. */
 TS_ATTN_API const char* ts_attn_strerror(int status);
 
+/* Build provenance (no counterpart in tensorsmith): SHA-256, as 64 hex digits,
+ * of the sources this library was compiled from -- every csrc/*.cu, csrc/*.cuh
+ * and include/*.h, hashed in file-name order as name, NUL, contents, NUL.  The
+ * Python loader refuses a library whose digest differs from the tree's. */
+TS_ATTN_API const char* ts_attn_source_digest(void);
+
 /* Kernel family ts_attn_fwd / ts_attn_decode would select (ts_fwd_path), or a
  * negative ts_status when the parameters are invalid. */
 TS_ATTN_API int ts_attn_fwd_path(const ts_attn_params* params, int decode);
@@ -151,7 +157,9 @@ TS_ATTN_API size_t ts_attn_decode_workspace_size(const ts_attn_params* params);
 
 /* Cached decode: a few query tokens against a long KV cache, split along the
  * keys and combined.  Same semantics as ts_attn_fwd; replaces the cached call
- * of nn/transformer.py:144-154 into nn/attention.py:132-145. */
+ * of nn/transformer.py:144-154 into nn/attention.py:132-145.  Problems the
+ * split-K kernels do not take (ts_attn_fwd_path(params, 1) != TS_PATH_DECODE)
+ * run exactly as ts_attn_fwd and need no workspace. */
 TS_ATTN_API int ts_attn_decode(const ts_attn_params* params, void* workspace, size_t workspace_bytes,
                    void* stream);
 
@@ -187,9 +195,10 @@ TS_ATTN_API int ts_kv_reorder(ts_view4 src, ts_view4 dst, int32_t dtype, int32_t
  * synchronise the device) between decode steps.  Same semantics and kernels as
  * ts_attn_decode, but the split partials live in a fixed library-owned device
  * array of TS_ATTN_NOALLOC_SCRATCH_BYTES on every GPU that loads the library,
- * held until exit.  The first call on a device looks up the array's device
- * address (make it before any stream capture); calls that overlap on the GPU
- * share the array and race.  Returns TS_ERR_WORKSPACE, launching nothing, when
+ * held until exit.  The first call in a CUDA context looks up the array's
+ * device address (make it before any stream capture; a context recreated after
+ * cudaDeviceReset looks it up again); calls that overlap on the GPU share the
+ * array and race.  Returns TS_ERR_WORKSPACE, launching nothing, when
  * the problem needs more scratch than that.  Allocates nothing. */
 TS_ATTN_API int ts_attn_decode_noalloc(const ts_attn_params* params, void* stream);
 
@@ -207,14 +216,14 @@ typedef struct ts_dropout {
 
 /* ts_attn_fwd with dropout: the tcgen05 kernel where ts_attn_fwd would use it,
  * the generic CUDA-core kernels otherwise (every dtype / shape / mask of
- * ts_attn_fwd).  p = 0 is the plain forward on the generic kernels. */
+ * ts_attn_fwd).  p = 0 is exactly ts_attn_fwd (same kernel selection). */
 TS_ATTN_API int ts_attn_fwd_dropout(const ts_attn_params* params, const ts_dropout* dropout, void* stream);
 
 /* Workspace bytes ts_attn_bwd_dropout needs. */
 TS_ATTN_API size_t ts_attn_bwd_dropout_workspace_size(const ts_attn_bwd_params* params);
 
 /* ts_attn_bwd for a forward made by ts_attn_fwd_dropout with the same dropout
- * arguments. */
+ * arguments (p = 0 is exactly ts_attn_bwd). */
 TS_ATTN_API int ts_attn_bwd_dropout(const ts_attn_bwd_params* params, const ts_dropout* dropout, void* workspace,
                                     size_t workspace_bytes, void* stream);
 

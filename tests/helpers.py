@@ -2,6 +2,9 @@
 
 from __future__ import annotations
 
+import json
+import os
+
 import numpy as np
 
 try:
@@ -16,9 +19,25 @@ TOL = {
     "float32": dict(rtol=1e-4, atol=2e-5),
     "float64": dict(rtol=1e-9, atol=1e-11),
 }
-# fp16 / bf16: max-abs error <= 2e-2 against the fp32 reference on the same (rounded)
-# inputs, measured relative to the reference's own scale max(1, max|ref|).
+# fp16 / bf16 (the north star's bound): max-abs error <= 2e-2 against the reference
+# computed in fp64 on the same rounded inputs.  Outputs and LSE are held to it as an
+# absolute bound.  Gradients (grad=True) are held to 2e-2 * max(1, max|ref|): dK / dV sum
+# over up to Tq query rows and grow past 1 at long sequences, where their bf16 storage
+# alone rounds by more than 2e-2; the errors measured at the benchmarked shapes are
+# recorded beside the kernels' description.
 HALF_MAXABS = 2e-2
+
+# When TS_PARITY_LOG names a file, every comparison appends one JSON line
+# {"what", "dtype", "max_abs", "max_ref", "bound"} to it (the measured errors).
+_PARITY_LOG = os.environ.get("TS_PARITY_LOG")
+
+
+def _log(what, name, err, max_ref, bound):
+    if not _PARITY_LOG:
+        return
+    with open(_PARITY_LOG, "a") as fh:
+        fh.write(json.dumps({"what": what, "dtype": name, "max_abs": err, "max_ref": max_ref,
+                             "bound": bound}) + "\n")
 
 
 def np_dtype(name):
@@ -57,18 +76,23 @@ def to_np(t) -> np.ndarray:
     return t.cpu().numpy()
 
 
-def assert_close(got, ref, name: str, what: str = ""):
+def assert_close(got, ref, name: str, what: str = "", *, grad: bool = False):
+    """fp32 / fp64: relative tolerance (TOL).  fp16 / bf16: max-abs <= 2e-2 for outputs and
+    LSE, 2e-2 * max(1, max|ref|) for gradients (``grad=True``)."""
     got = np.asarray(got, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
     assert got.shape == ref.shape, (what, got.shape, ref.shape)
     finite = np.isfinite(ref)
     assert np.array_equal(np.isfinite(got), finite), f"{what}: non-finite pattern differs"
+    err = float(np.max(np.abs(got[finite] - ref[finite]))) if finite.any() else 0.0
+    max_ref = float(np.max(np.abs(ref[finite]))) if finite.any() else 0.0
     if name in TOL:
+        _log(what, name, err, max_ref, "rtol=%g atol=%g" % (TOL[name]["rtol"], TOL[name]["atol"]))
         np.testing.assert_allclose(got[finite], ref[finite], err_msg=what, **TOL[name])
     else:
-        scale = max(1.0, float(np.max(np.abs(ref[finite]))) if finite.any() else 1.0)
-        err = float(np.max(np.abs(got[finite] - ref[finite]))) if finite.any() else 0.0
-        assert err <= HALF_MAXABS * scale, f"{what}: max-abs {err:.3e} > {HALF_MAXABS}*{scale:.3g}"
+        bound = HALF_MAXABS * (max(1.0, max_ref) if grad else 1.0)
+        _log(what, name, err, max_ref, bound)
+        assert err <= bound, f"{what}: max-abs {err:.3e} > {bound:.3g}"
 
 
 def oracle_forward(q, k, v, **kw):

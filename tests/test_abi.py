@@ -102,3 +102,9 @@ def test_invalid_arguments_rejected_without_launch():
     assert handle.ts_kv_append(ctypes.byref(a), None) == _lib.ERR_INVALID_ARGUMENT
     bp = _lib.AttnBwdParams()
     assert handle.ts_attn_bwd(ctypes.byref(bp), None, 0, None) == _lib.ERR_INVALID_ARGUMENT
+
+
+def test_library_was_built_from_this_tree():
+    # ts_attn_source_digest: the loader refuses a library built from other sources.
+    assert _lib.library_digest() == _lib.source_digest()
+    assert len(_lib.source_digest()) == 64

@@ -66,9 +66,23 @@ def _worker(rank, world, port, queue):
             works.append(gather_to_root(local[:, c0 : c0 + 2], plan, out=targets, async_op=True))
         for work in works:
             work.wait()
+        # asynchronously into one contiguous full buffer
+        whole = torch.zeros(world * plan.size, t, d).reshape(world, plan.size, t, d) if rank == 0 else None
+        work = gather_to_root(local, plan, out=whole, async_op=True)
+        work.wait()
+        # an asynchronous call on the root without `out` would lose its result
+        refused = True
+        if rank == 0:
+            try:
+                gather_to_root(local, plan, async_op=True)
+                refused = False
+            except ValueError:
+                pass
+        dist.barrier()
         if rank == 0:
             queue.put(("ok", torch.equal(out.reshape(b, h, t, d), full)
-                       and torch.equal(blocks.reshape(b, h, t, d), full)))
+                       and torch.equal(blocks.reshape(b, h, t, d), full)
+                       and torch.equal(whole.reshape(b, h, t, d), full) and refused))
         else:
             queue.put(("ok", out is None))
     except Exception as error:  # pragma: no cover - reported to the parent
@@ -88,3 +102,15 @@ def test_gather_to_root_world2():
     for p in procs:
         p.join(timeout=30)
     assert all(kind == "ok" and flag for kind, flag in results), results
+
+
+def test_gather_to_root_single_rank():
+    plan = ShardPlan(2, 2, 1, 0)
+    local = torch.arange(2 * 2 * 3 * 4, dtype=torch.float32).reshape(2, 2, 3, 4)
+    assert gather_to_root(local, plan) is local
+    out = torch.empty_like(local)
+    assert gather_to_root(local, plan, out=out) is out and torch.equal(out, local)
+    out2 = torch.empty_like(local)
+    assert gather_to_root(local, plan, out=out2, async_op=True) is None and torch.equal(out2, local)
+    with pytest.raises(ValueError):
+        gather_to_root(local, plan, async_op=True)

@@ -83,7 +83,7 @@ def test_dropout_forward_backward_match_oracle(case, p):
     # The backward's Delta uses the stored (dtype-rounded) output, as the engine does.
     rdq, rdk, rdv = oracle.attention_backward_dense(qr, kr, vr, gr, host_mask, **okw)
     for got, ref, what in ((dq, rdq, "dq"), (dk, rdk, "dk"), (dvv, rdv, "dv")):
-        assert_close(to_np(got), ref, name, f"dropout {what}")
+        assert_close(to_np(got), ref, name, f"dropout {what}", grad=True)
 
 
 def test_dropout_zero_probability_equals_plain_forward():
@@ -155,4 +155,4 @@ def test_tcgen05_dropout_matches_oracle(case):
     assert_close(to_np(lse), ref_l, "float32", "tc dropout lse")
     rdq, rdk, rdv = oracle.attention_backward_dense(qr, kr, vr, gr, None, **okw)
     for got, ref, what in ((dq, rdq, "dq"), (dk, rdk, "dk"), (dvv, rdv, "dv")):
-        assert_close(to_np(got), ref, name, f"tc dropout {what}")
+        assert_close(to_np(got), ref, name, f"tc dropout {what}", grad=True)
