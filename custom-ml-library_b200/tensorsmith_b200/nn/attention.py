@@ -4,7 +4,8 @@ Signature, argument meaning, validation order, exception types and messages
 follow tensorsmith's src/tensorsmith/nn/attention.py:16-87; the compute behind
 it is the engine (tcgen05 prefill, CUDA-core generic path, split-K decode) and
 the VJP is the engine's recomputing backward, recorded as one tape node like
-nn/attention.py:250-252.  Every ``backend`` string routes to the engine on
+nn/attention.py:250-252 (``tensorsmith_b200.interop.attention_node``, which
+works with tensorsmith's own Tensor class as well as the torch-backed mirror).  Every ``backend`` string routes to the engine on
 CUDA (all of them are exact attention); there is no host fallback.
 """
 
@@ -12,7 +13,7 @@ from __future__ import annotations
 
 import math
 
-from .. import engine
+from .. import engine, interop
 from ..tensor import Tensor, is_grad_enabled
 
 BACKENDS = {"auto", "dense", "streaming", "native"}
@@ -88,34 +89,10 @@ def scaled_dot_product_attention(
         raise ValueError("attention dropout currently requires the dense backend")
 
     recording = is_grad_enabled() and any(t.requires_grad for t in (query, key, value))
-    q, k, v = query._data, key._data, value._data
-    kwargs = dict(is_causal=is_causal, scale=multiplier, causal_offset=causal_offset,
-                  kv_lens=kv_lens, mask=mask)
-    if dropout_p:
-        # One draw of the generator per call; the backward reuses it (nn/attention.py:140-144, 212-216).
-        kwargs["dropout"] = engine.DROPOUT_GENERATOR.draw(dropout_p)
-        output, lse = engine.forward(q, k, v, need_lse=True, **kwargs)
-        if not recording:
-            return Tensor(output, device=query.device)
-
-        def backward_dropout(upstream):
-            return engine.backward(q, k, v, output, lse, upstream, **kwargs)
-
-        return Tensor._from_op(output, (query, key, value), backward_dropout, "sdpa_" + selected)
-    if not recording:
-        if repetitions * qlen <= engine.DECODE_MAX_ROWS and mask is None:
-            output, _ = engine.decode(q, k, v, **kwargs)
-        else:
-            output, _ = engine.forward(q, k, v, need_lse=False, **kwargs)
-        return Tensor(output, device=query.device)
-
-    output, lse = engine.forward(q, k, v, need_lse=True, **kwargs)
-
-    def backward(upstream):
-        dq, dk, dv = engine.backward(q, k, v, output, lse, upstream, **kwargs)
-        return dq, dk, dv
-
-    return Tensor._from_op(output, (query, key, value), backward, "sdpa_" + selected)
+    dropout = engine.DROPOUT_GENERATOR.draw(dropout_p) if dropout_p else None  # one draw per call
+    return interop.attention_node(query, key, value, mask=mask, is_causal=is_causal, scale=multiplier,
+                                  causal_offset=causal_offset, kv_lens=kv_lens, dropout=dropout,
+                                  op="sdpa_" + selected, recording=recording, decode_rows=repetitions * qlen)
 
 
 def rotary_embedding(input: Tensor, offset: int = 0, base: float = 10000.0, rotary_dim: int | None = None) -> Tensor:

@@ -2,12 +2,13 @@
 
 The engine's attention op records exactly one node per call through
 ``Tensor._from_op(data, parents, backward, op)``, the interface of
-tensorsmith's src/tensorsmith/tensor.py:121-135; ``backward`` runs the
-reverse-topological VJP sweep of tensor.py:247-267 / :662-724 (contributions
-summed per parent, cast to the parent's dtype).  This mirror carries torch
-CUDA arrays in ``_data`` so the engine can be driven and tested without CuPy;
-inside tensorsmith itself the same closure is handed to the library's own
-``Tensor._from_op``.
+tensorsmith's src/tensorsmith/tensor.py:121-135; ``backward`` runs a reverse
+sweep with that tape's contract (tensor.py:247-267, :662-724: contributions
+summed per tensor and cast to its dtype, one VJP call per node), implemented
+here by consumer counting.  This mirror carries torch CUDA arrays in
+``_data`` so the engine can be driven and tested without CuPy; inside
+tensorsmith itself ``tensorsmith_b200.interop.attention_node`` hands the same
+kind of node to the library's own ``Tensor._from_op``.
 """
 
 from __future__ import annotations
@@ -195,42 +196,55 @@ class Tensor:
 
 
 def _run_backward(root: Tensor, seed, *, retain_graph: bool = False) -> None:
-    order, seen = [], set()
-    stack = [(root, False)]
-    while stack:
-        node, expanded = stack.pop()
-        if expanded:
-            order.append(node)
-            continue
-        if id(node) in seen:
-            continue
-        seen.add(id(node))
-        stack.append((node, True))
-        stack.extend((parent, False) for parent in node._parents)
-    pending = {id(root): seed}
-    for node in reversed(order):
-        contribution = pending.pop(id(node), None)
-        if contribution is None:
-            continue
-        if node.requires_grad and contribution.dtype != node.dtype:
-            contribution = contribution.to(node.dtype)
-        if node.requires_grad:
-            node._grad = contribution if node._grad is None else node._grad + contribution
-        if node._backward is not None:
-            grads = node._backward(contribution)
-            if len(grads) != len(node._parents):
-                raise RuntimeError(f"internal error: {node._op} returned wrong number of gradients")
-            for parent, g in zip(node._parents, grads):
-                if g is None or not parent.requires_grad:
-                    continue
+    """Reverse sweep from ``root`` under the tape contract of ``_from_op``.
+
+    Contract (tensorsmith's tape): every recorded use of a tensor sends it one
+    gradient contribution; the contributions of all its uses are summed and
+    cast to the tensor's dtype before they are stored in ``_grad`` and handed
+    to the tensor's own VJP, which returns one contribution (or None) per
+    parent.  Here a tensor is processed once every consumer edge into it has
+    delivered (consumer counting), so each VJP runs exactly once with its
+    complete gradient.  Without ``retain_graph`` the recorded graph is released.
+    """
+    # Consumer edges per tensor reachable from the root.
+    pending_uses: dict[int, int] = {}
+    reachable: list[Tensor] = [root]
+    seen = {id(root)}
+    for node in reachable:  # grows while iterating: a breadth-first walk
+        if node._graph_freed:
+            raise RuntimeError("this autograd tape has already been freed")
+        for parent in node._parents:
+            pending_uses[id(parent)] = pending_uses.get(id(parent), 0) + 1
+            if id(parent) not in seen:
+                seen.add(id(parent))
+                reachable.append(parent)
+    summed = {id(root): seed}
+    ready = [root]
+    while ready:
+        node = ready.pop()
+        grad = summed.pop(id(node), None)
+        if grad is not None and node.requires_grad:
+            if grad.dtype != node.dtype:
+                grad = grad.to(node.dtype)
+            node._grad = grad if node._grad is None else node._grad + grad
+        parent_grads = None
+        if grad is not None and node._backward is not None:
+            parent_grads = tuple(node._backward(grad))
+            if len(parent_grads) != len(node._parents):
+                raise RuntimeError(
+                    f"{node._op}: backward gave {len(parent_grads)} gradients for {len(node._parents)} inputs")
+        for index, parent in enumerate(node._parents):
+            contribution = None if parent_grads is None else parent_grads[index]
+            if contribution is not None and parent.requires_grad:
                 key = id(parent)
-                pending[key] = g if key not in pending else pending[key] + g
+                summed[key] = contribution if key not in summed else summed[key] + contribution
+            pending_uses[id(parent)] -= 1
+            if pending_uses[id(parent)] == 0:
+                ready.append(parent)
     if not retain_graph:
-        for node in order:
+        for node in reachable:
             if node._backward is not None:
-                node._parents = ()
-                node._backward = None
-                node._graph_freed = True
+                node._parents, node._backward, node._graph_freed = (), None, True
 
 
 def tensor(data, **kwargs) -> Tensor:

@@ -30,6 +30,12 @@ file:line of the behaviour each pins):
   fp64, with the keep mask the reference drew (nn/attention.py:140-144,
   212-216; device.py:276-297 -- on the CPU backend the draw is
   ``np.random.random(shape).astype(float32)`` right after the seed)
+* ``lm``          a 2-layer TransformerLM (vocab 64, dim 32, 4 query heads over
+  2 KV heads, RoPE) in eval mode: its weights, full-prefix logits, chunked
+  cached logits (chunks 5/1/3), ``logits_to_keep=1``, int8-cache logits,
+  16 greedy tokens with and without the cache, and one fp32 training step's
+  loss and parameter gradients (nn/transformer.py:85-155, 262-402;
+  tests/test_transformer.py:287-381)
 
 ``--only NAME`` regenerates one case and leaves the other files untouched.
 """
@@ -232,14 +238,52 @@ def run_dropout(reference_src: str) -> None:
     np.savez_compressed(HERE / "dropout.npz", **case)
 
 
+def run_lm(reference_src: str) -> None:
+    sys.path.insert(0, reference_src)
+    import tensorsmith as ts
+    from tensorsmith import nn
+
+    np.random.seed(71)  # the reference initialises parameters from NumPy's global generator
+    config = nn.TransformerConfig(64, dim=32, num_heads=4, num_kv_heads=2, num_layers=2, max_seq_len=32)
+    model = nn.TransformerLM(config).eval()
+    case = {f"param:{name}": np.asarray(value) for name, value in model.state_dict().items()}
+    tokens = np.random.default_rng(72).integers(0, 64, (2, 9))
+    case["tokens"] = tokens
+    with ts.no_grad():
+        case["logits_full"] = model(ts.tensor(tokens)).numpy()
+        case["logits_keep1"] = model(ts.tensor(tokens), logits_to_keep=1).numpy()
+        caches = model.new_cache(2)
+        chunks = [model(ts.tensor(tokens[:, a:b]), caches=caches).numpy() for a, b in ((0, 5), (5, 6), (6, 9))]
+        case["logits_chunked"] = np.concatenate(chunks, axis=1)
+        case["cache_lengths"] = np.array([c.length for c in caches])
+        case["logits_int8_cache"] = model(ts.tensor(tokens), caches=model.new_cache(2, quantized=True)).numpy()
+    prompt = tokens[:, :3]
+    case["greedy_cached"] = model.generate(ts.tensor(prompt), 16, temperature=0).numpy()
+    case["greedy_uncached"] = model.generate(ts.tensor(prompt), 16, temperature=0, use_cache=False).numpy()
+    # one training step in fp32 (dropout 0): loss and every parameter's gradient
+    model.train()
+    targets = np.random.default_rng(73).integers(0, 64, (2, 9))
+    case["targets"] = targets
+    loss = model.loss(ts.tensor(tokens), ts.tensor(targets))
+    loss.backward()
+    case["loss"] = np.float64(loss.item())
+    for name, param in model.named_parameters():
+        case[f"grad:{name}"] = param.grad.numpy()
+    np.savez_compressed(HERE / "lm.npz", **case)
+
+
 def main():
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--reference", required=True, help="path to the tensorsmith src directory")
-    parser.add_argument("--only", default=None, help="regenerate one case (dropout)")
+    parser.add_argument("--only", default=None, help="regenerate one case (dropout, lm)")
     args = parser.parse_args()
     if args.only == "dropout":
         run_dropout(args.reference)
         return
+    if args.only == "lm":
+        run_lm(args.reference)
+        return
+    run_lm(args.reference)
     run_dropout(args.reference)
     meta = run(args.reference)
     (HERE / "meta.json").write_text(json.dumps(meta, indent=2) + "\n")

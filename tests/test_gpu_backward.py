@@ -43,9 +43,9 @@ def test_backward(shape, name):
     dq, dk, dv_ = engine.backward(tq_, tk_, tv_, out, lse, tg, is_causal=causal, causal_offset=off)
     torch.cuda.synchronize()
     engine.check_device_status()
-    assert_close(to_np(dq), rdq, name, f"dq {shape}", grad=True)
-    assert_close(to_np(dk), rdk, name, f"dk {shape}", grad=True)
-    assert_close(to_np(dv_), rdv, name, f"dv {shape}", grad=True)
+    assert_close(to_np(dq), rdq, name, f"dq {shape}", scaled=True)
+    assert_close(to_np(dk), rdk, name, f"dk {shape}", scaled=True)
+    assert_close(to_np(dv_), rdv, name, f"dv {shape}", scaled=True)
 
 
 @pytest.mark.parametrize("kind", ["bool", "float"])
@@ -91,9 +91,9 @@ def test_backward_tcgen05(shape, name):
     dq, dk, dv_ = engine.backward(tq_, tk_, tv_, out, lse, tg, is_causal=causal, causal_offset=off)
     torch.cuda.synchronize()
     engine.check_device_status()
-    assert_close(to_np(dq), rdq, name, f"dq {shape}", grad=True)
-    assert_close(to_np(dk), rdk, name, f"dk {shape}", grad=True)
-    assert_close(to_np(dv_), rdv, name, f"dv {shape}", grad=True)
+    assert_close(to_np(dq), rdq, name, f"dq {shape}", scaled=True)
+    assert_close(to_np(dk), rdk, name, f"dk {shape}", scaled=True)
+    assert_close(to_np(dv_), rdv, name, f"dv {shape}", scaled=True)
 
 
 def test_backward_tcgen05_kv_lens_and_btdh_views():
@@ -113,6 +113,6 @@ def test_backward_tcgen05_kv_lens_and_btdh_views():
         # keys past the row's length are masked; queries sit at the end of the valid keys
         mask = np.arange(t)[None, None, None, :] < n
         _, _, (rdq, rdk, rdv) = oracle_backward(qn, kn, vn, gn, mask=mask, is_causal=True, causal_offset=n - t)
-        assert_close(to_np(dq[row : row + 1]), rdq, "bfloat16", f"dq row {row}", grad=True)
-        assert_close(to_np(dk[row : row + 1]), rdk, "bfloat16", f"dk row {row}", grad=True)
-        assert_close(to_np(dv_[row : row + 1]), rdv, "bfloat16", f"dv row {row}", grad=True)
+        assert_close(to_np(dq[row : row + 1]), rdq, "bfloat16", f"dq row {row}", scaled=True)
+        assert_close(to_np(dk[row : row + 1]), rdk, "bfloat16", f"dk row {row}", scaled=True)
+        assert_close(to_np(dv_[row : row + 1]), rdv, "bfloat16", f"dv row {row}", scaled=True)

@@ -110,9 +110,9 @@ def test_c3_forward_backward_full_slices():
         tag = f"(b={b}, h={h})"
         assert_close(to_np(out[b, h])[None, None], ref_o, "bfloat16", f"c3 out {tag}")
         assert_close(to_np(lse[b, h])[None, None], ref_l, "bfloat16", f"c3 lse {tag}")
-        assert_close(to_np(dq[b, h])[None, None], rdq, "bfloat16", f"c3 dq {tag}", grad=True)
-        assert_close(to_np(dk[b, h])[None, None], rdk, "bfloat16", f"c3 dk {tag}", grad=True)
-        assert_close(to_np(dv[b, h])[None, None], rdv, "bfloat16", f"c3 dv {tag}", grad=True)
+        assert_close(to_np(dq[b, h])[None, None], rdq, "bfloat16", f"c3 dq {tag}", scaled=True)
+        assert_close(to_np(dk[b, h])[None, None], rdk, "bfloat16", f"c3 dk {tag}", scaled=True)
+        assert_close(to_np(dv[b, h])[None, None], rdv, "bfloat16", f"c3 dv {tag}", scaled=True)
 
 
 @pytest.mark.parametrize("kv_heads,quantized", [(32, False), (8, False), (32, True)],

@@ -83,7 +83,7 @@ def test_dropout_forward_backward_match_oracle(case, p):
     # The backward's Delta uses the stored (dtype-rounded) output, as the engine does.
     rdq, rdk, rdv = oracle.attention_backward_dense(qr, kr, vr, gr, host_mask, **okw)
     for got, ref, what in ((dq, rdq, "dq"), (dk, rdk, "dk"), (dvv, rdv, "dv")):
-        assert_close(to_np(got), ref, name, f"dropout {what}", grad=True)
+        assert_close(to_np(got), ref, name, f"dropout {what}", scaled=True)
 
 
 def test_dropout_zero_probability_equals_plain_forward():
@@ -100,7 +100,7 @@ def test_sdpa_dropout_api_and_tape():
     rng = np.random.default_rng(8)
     raw = [rng.normal(size=(1, 2, 6, 8)).astype(np.float32) for _ in range(3)]
     up = rng.normal(size=(1, 2, 6, 8)).astype(np.float32)
-    tensors = [ts.Tensor(torch.from_numpy(a).cuda(), requires_grad=True) for a in raw]
+    tensors = [ts.Tensor(torch.from_numpy(a).cuda(), requires_scaled=True) for a in raw]
     ts.seed(8)
     out = nn.scaled_dot_product_attention(*tensors, dropout_p=0.3, is_causal=True)
     out.backward(ts.Tensor(torch.from_numpy(up).cuda()))
@@ -155,4 +155,4 @@ def test_tcgen05_dropout_matches_oracle(case):
     assert_close(to_np(lse), ref_l, "float32", "tc dropout lse")
     rdq, rdk, rdv = oracle.attention_backward_dense(qr, kr, vr, gr, None, **okw)
     for got, ref, what in ((dq, rdq, "dq"), (dk, rdk, "dk"), (dvv, rdv, "dv")):
-        assert_close(to_np(got), ref, name, f"tc dropout {what}", grad=True)
+        assert_close(to_np(got), ref, name, f"tc dropout {what}", scaled=True)

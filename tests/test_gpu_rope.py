@@ -43,7 +43,7 @@ def test_rope_matches_oracle(name, offset, dim):
     # the inverse rotation undoes the rotation (up to storage rounding)
     back = to_np(engine.rope(engine.rope(to_cuda(x, name), offset=offset, rotary_dim=dim), offset=offset,
                              rotary_dim=dim, inverse=True))
-    assert_close(back, x, name if name not in ROPE_TOL else "bfloat16", "inverse")
+    assert_close(back, x, name if name not in ROPE_TOL else "bfloat16", "inverse", scaled=True)
 
 
 def test_rope_golden_and_vjp(golden):
