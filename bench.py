@@ -48,6 +48,8 @@ WORKLOADS = {
     "c5slice": dict(batch=1, heads=8, head_dim=128, prefill=32768, scale_inputs=False),
     # causal prefill bf16 forward + backward
     "c3": dict(batch=8, heads=16, head_dim=128, prefill=4096, scale_inputs=True),
+    # 4-layer decoder LM training step (fp16 autocast, fp32 params), B=16, T=256
+    "c2": dict(batch=16, seq=256, vocab=8192, dim=256, heads=4, layers=4, hidden=1024),
     # fp16 KV-cache decode, ragged lengths U[1024, 8192], 256 steps with append
     "c4": dict(batch=64, heads=32, head_dim=128, min_len=1024, max_len=8192, decode_steps=256),
     # config 3 with the int8 KV cache (KVCache(quantized=True)): quantising append + fused-dequant decode
@@ -57,7 +59,31 @@ WORKLOADS = {
     # reduced c4q (0.55 GB int8 cache, still larger than L2), for profiler captures only
     "c4q_small": dict(batch=8, heads=32, head_dim=128, min_len=1024, max_len=8192, decode_steps=16),
 }
+# Query rows per prefill chunk when N > 1 (each chunk's output gather overlaps the next chunk).
+PREFILL_CHUNK_ROWS = 4096
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the scored kernel, from the ncu
+# captures summarised under profiles/, per unit of work so a launch of any size scales by its units.
+PROFILED_TRAFFIC = {
+    # tc_fwd_kernel<128,bf16> at T=32768, 8 (b,h) pairs: (201.4 + 51.3) MB / 8 pairs
+    "c5": dict(bytes_per_unit=31.59e6, unit="(b,h) pair at T=32768",
+               source="profiles/tc_fwd_bwd_kernels_c5slice.md"),
+    # tc_bwd_kernel<128,bf16> at the C3 shape: 809.7 MB read + 493.0 MB written per launch
+    "c3": dict(bytes_per_unit=1302.7e6, unit="C3 backward launch", source="profiles/tc_bwd_kernel_c3.md"),
+    # split-K decode: DRAM bytes / algorithmic K+V bytes = (268.6 + 4.1) / 268.5
+    "c4": dict(bytes_per_unit=1.0156, unit="algorithmic K+V byte", source="profiles/decode_split_kernel_small.md"),
+    # grouped decode: (1348.6 + 8.1) / 1340 (algorithmic K+V bytes of that step)
+    "c4gqa": dict(bytes_per_unit=1.0125, unit="algorithmic K+V byte", source="profiles/decode_group_kernel_c4gqa.md"),
+}
+
+
+def profiled_traffic(key: str, units: float):
+    """Per-launch DRAM traffic scaled from a committed ncu capture, or None."""
+    entry = PROFILED_TRAFFIC.get(key)
+    if entry is None:
+        return None
+    return {"bytes": entry["bytes_per_unit"] * units, "per": entry["unit"], "units": units,
+            "source": entry["source"] + " (ncu capture, scaled by the units of this launch)"}
 CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -292,7 +318,7 @@ def run_reference(args, rank: int, world: int):
 # --------------------------------------------------------------------------
 # engine arm
 # --------------------------------------------------------------------------
-def parity_c5(q, kc, vc, o, qd, od, T, S, D, seed=7):
+def parity_c5(q, kc, vc, prefill_rows, qd, od, T, S, D, seed=7):
     """Sampled check of the timed step's outputs on this rank: the first and last (b,h) pair,
     the last 128 prefill rows plus 128 random ones, and decode steps 0 and S-1."""
     import torch
@@ -305,7 +331,7 @@ def parity_c5(q, kc, vc, o, qd, od, T, S, D, seed=7):
     for pr in sorted({0, n - 1}):
         kh, vh = kc[0, pr, : T + S].cpu(), vc[0, pr, : T + S].cpu()
         ref, _ = ref_rows(q[0, pr].cpu()[rows], kh[:T], vh[:T], rows + 1, scale)
-        err_o = max(err_o, max_abs(o[0, pr].cpu()[rows], ref))
+        err_o = max(err_o, max_abs(prefill_rows(pr)[rows], ref))
         for st in sorted({0, S - 1}):
             ref_d, _ = ref_rows(qd[st, 0, pr].cpu(), kh, vh, [T + st + 1], scale)
             err_d = max(err_d, max_abs(od[st, 0, pr].cpu(), ref_d))
@@ -342,12 +368,11 @@ def run_engine(args, rank: int, world: int, local_rank: int):
     vc = torch.zeros_like(kc)
     kc[:, :, :T].copy_(randn(1, n, T, D))
     vc[:, :, :T].copy_(randn(1, n, T, D))
-    o = torch.empty(1, n, T, D, dtype=bf, device=dev)
+    o = torch.empty(1, n, T, D, dtype=bf, device=dev) if world == 1 else None
     qd = randn(S, 1, n, 1, D)
     kd = randn(S, 1, n, 1, D)
     vd = randn(S, 1, n, 1, D)
     od = torch.empty(S, 1, n, 1, D, dtype=bf, device=dev)
-    o_full = torch.empty(world, n, T, D, dtype=bf, device=dev) if rank == 0 and world > 1 else None
     od_full = torch.empty(S, world, n, 1, D, dtype=bf, device=dev) if rank == 0 and world > 1 else None
     ws = torch.empty(max(16, engine.decode_workspace_bytes(qd[0], kc[:, :, : T + 1], vc[:, :, : T + 1],
                                                              is_causal=True, causal_offset=T)),
@@ -356,11 +381,27 @@ def run_engine(args, rank: int, world: int, local_rank: int):
 
     splits = engine.decode_workspace_bytes(qd[0], kc[:, :, :cap], vc[:, :, :cap], is_causal=True,
                                            causal_offset=cap - 1) > 0
-    # With N > 1 each decode token's gather is queued on the process group's
-    # stream and waited for at the end of the step, so it overlaps the next
-    # token's append and decode.  (Splitting the prefill into blocks of pairs to
-    # overlap its gather costs more in per-block causal tails than it saves.)
-    launches_per_step = 1 + S * (2 + (1 if splits else 0))
+    # With N > 1 the prefill runs in query-row chunks, longest first, and each
+    # chunk's output is gathered asynchronously (on the process group's stream)
+    # while the next chunk computes; the step waits for the gathers before the
+    # decode loop.  The CTAs of one chunk have similar causal lengths, so the
+    # chunks add little tail (splitting by blocks of pairs instead costs a full
+    # causal tail per block).  Rank 0 receives chunk c of every rank in
+    # o_full_parts[c] ([world, pairs, rows_c, D]).  One GPU runs one launch.
+    # Each decode token's gather is queued the same way and waited for at the
+    # end of the step, so it overlaps the next token's append and decode.
+    rows_per_chunk = T if world == 1 else min(T, PREFILL_CHUNK_ROWS)
+    chunks = [(r0, min(T, r0 + rows_per_chunk)) for r0 in range(0, T, rows_per_chunk)][::-1]
+    o_parts = ([torch.empty(1, n, r1 - r0, D, dtype=bf, device=dev) for r0, r1 in chunks] if world > 1 else None)
+    o_full_parts = ([torch.empty(world, n, r1 - r0, D, dtype=bf, device=dev) for r0, r1 in chunks]
+                    if rank == 0 and world > 1 else None)
+    launches_per_step = len(chunks) + S * (2 + (1 if splits else 0))
+
+    def prefill_rows(pr):
+        """Prefill output rows of local pair ``pr`` on the host, [T, D]."""
+        if o_parts is None:
+            return o[0, pr].cpu()
+        return torch.cat([o_parts[c][0, pr].cpu() for c in sorted(range(len(chunks)), key=lambda c: chunks[c][0])])
 
     def gather(src, dst):
         if world > 1:
@@ -373,9 +414,17 @@ def run_engine(args, rank: int, world: int, local_rank: int):
 
     def step(ev):
         ev[0].record()
-        engine.forward(q, kc[:, :, :T], vc[:, :, :T], is_causal=True, need_lse=False, out=o)
+        works = []
+        if world == 1:
+            engine.forward(q, kc[:, :, :T], vc[:, :, :T], is_causal=True, need_lse=False, out=o)
+        else:
+            for c, (r0, r1) in enumerate(chunks):
+                engine.forward(q[:, :, r0:r1], kc[:, :, :r1], vc[:, :, :r1], is_causal=True, causal_offset=r0,
+                               need_lse=False, out=o_parts[c])
+                works.append(gather_async(o_parts[c], None if o_full_parts is None else o_full_parts[c]))
         ev[1].record()
-        gather(o, o_full)
+        for work in works:
+            work.wait()
         ev[2].record()
         works = []
         for s in range(S):
@@ -457,8 +506,9 @@ def run_engine(args, rank: int, world: int, local_rank: int):
             "config": {
                 "workload": (f"{args.workload}: causal prefill bf16 B={B} H={H} D={D} T={T}, then {S} decode "
                              f"steps (KV append + split-K decode), (b,h) pairs sharded over {world} GPU(s), "
-                             "outputs gathered to rank 0 over NCCL (decode gathers queued and waited for at the "
-                             "end of the step)"),
+                             "outputs gathered to rank 0 over NCCL (with N > 1 the prefill runs in "
+                             f"{len(chunks)} query-row chunks, longest first, each chunk's gather overlapping the "
+                             "next chunk; decode gathers queued and waited for at the end of the step)"),
                 "global_batch": B, "seq_len": T, "parallelism": f"bxh-shard{world}",
                 "l2": "inputs larger than L2 (Q/K/V/cache >= 8 GB per step)",
             },
@@ -472,14 +522,15 @@ def run_engine(args, rank: int, world: int, local_rank: int):
             "roofline": {"bound": "tensor", "kernel": "tc_fwd_kernel<128,bf16>", "achieved": achieved,
                          "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                          "peak_source": f"{peak_src} bf16_tflops_sustained",
-                         "traffic": None,
-                         "algorithmic": f"4*D*causal_pairs = {flops_rank:.4g} FLOP per launch on rank 0"},
+                         "traffic": profiled_traffic("c5", n) if T == 32768 else None,
+                         "algorithmic": f"4*D*causal_pairs = {flops_rank:.4g} FLOP per launch on rank 0; "
+                                        f"bytes Q+K+V read, O written = {4 * n * T * D * 2:.4g}"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
         }
         if e2e is not None:
             result["e2e"] = e2e
-        result["parity"] = parity_c5(q, kc, vc, o, qd, od, T, S, D)
+        result["parity"] = parity_c5(q, kc, vc, prefill_rows, qd, od, T, S, D)
         if world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
     return result
@@ -684,7 +735,8 @@ def run_c3(args):
                      "launches": "row-statistics preprocess + dQ accumulator memset + tc_bwd_kernel + dQ convert"},
         "roofline": {"bound": "tensor", "kernel": "backward call (tc_bwd_kernel dominant)", "achieved": bwd_tf,
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": bwd_tf / peaks["bf16_tflops"],
-                     "peak_source": f"{src} bf16_tflops (burst; the call runs ~ms)", "traffic": None,
+                     "peak_source": f"{src} bf16_tflops (burst; the call runs ~ms)",
+                     "traffic": profiled_traffic("c3", 1) if args.workload == "c3" else None,
                      "algorithmic": f"10*D*causal_pairs = {10 * pairs_flops:.4g} FLOP per backward call"},
         "gpu_launches": 4 * args.steps,  # tc_fwd_kernel, bwd_stats_kernel, tc_bwd_kernel, dq_convert_kernel
         "clocks": clocks,
@@ -692,6 +744,112 @@ def run_c3(args):
     if not args.no_cpu_baseline and args.workload == "c3":
         line["cpu_baseline"] = cpu_c3_baseline(cfg, args.cpu_seconds)
     return line
+
+
+def run_c2(args):
+    """decoder-only LM (4 layers, d_model 256, 4 heads of 64, FFN 1024, vocab 8192)
+    forward + backward under fp16 autocast with fp32 parameters, B=16, T=256, synthetic tokens.
+    The attention path (RoPE, attention forward and backward) runs on the engine; projections, norms,
+    the MLP and the loss are torch ops.  ``value`` is training tokens/s of the whole step; the
+    ``attention`` object times the engine's attention forward + backward at the step's shapes."""
+    import numpy as np
+    import torch
+
+    from tensorsmith_b200 import engine, nn
+
+    cfg = WORKLOADS["c2"]
+    B, T, V, E, H, L = cfg["batch"], cfg["seq"], cfg["vocab"], cfg["dim"], cfg["heads"], cfg["layers"]
+    D = E // H
+    np.random.seed(11)
+    model = nn.TransformerLM(nn.TransformerConfig(V, dim=E, num_heads=H, num_layers=L, hidden_dim=cfg["hidden"],
+                                                  max_seq_len=T), device="cuda").train()
+    params = model.parameters()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(12)
+    tokens = torch.randint(0, V, (B, T + 1), generator=gen, device="cuda")
+
+    def step(ev):
+        ev[0].record()
+        for prm in params:
+            prm.grad = None
+        with torch.autocast("cuda", dtype=torch.float16):
+            loss = model.loss(tokens[:, :-1], tokens[:, 1:])
+        loss.backward()
+        ev[1].record()
+
+    evs, step_ms, clocks = _timed(args, step, 2)
+    ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    # the engine's attention alone at the step's shapes (fp16 q/k/v as autocast hands them over)
+    q, k, v, g = (torch.randn(B, H, T, D, generator=gen, device="cuda").half() for _ in range(4))
+    out, lse = engine.forward(q, k, v, is_causal=True)
+
+    def attn(ev):
+        ev[0].record()
+        for _ in range(L):
+            o, l = engine.forward(q, k, v, is_causal=True, out=out, lse=lse)
+        ev[1].record()
+        for _ in range(L):
+            engine.backward(q, k, v, out, lse, g, is_causal=True)
+        ev[2].record()
+
+    aevs, _, _ = _timed(args, attn, 3)
+    a_fwd = statistics.mean(e[0].elapsed_time(e[1]) for e in aevs)
+    a_bwd = statistics.mean(e[1].elapsed_time(e[2]) for e in aevs)
+    dp = causal_flops(B * H, T, T, 0, D) / 4.0 * L  # D * causal pairs over the layers
+    # parity of one attention call at this shape (sampled (b,h) slice in full, fp64 on the host)
+    dq, dk, dv = engine.backward(q, k, v, out, lse, g, is_causal=True)
+    ro, rl, rdq, rdk, rdv = ref_slice_backward(q[-1, -1].cpu(), k[-1, -1].cpu(), v[-1, -1].cpu(), g[-1, -1].cpu(),
+                                               D ** -0.5)
+    errs = {"out": max_abs(out[-1, -1], ro), "dq": max_abs(dq[-1, -1], rdq), "dk": max_abs(dk[-1, -1], rdk),
+            "dv": max_abs(dv[-1, -1], rdv)}
+    peaks, src = load_peaks()
+    line = {
+        "metric": METRIC, "value": B * T / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"c2: decoder LM {L} layers, d_model {E}, {H} heads x {D}, FFN {cfg['hidden']}, "
+                               f"vocab {V}, B={B} T={T}, fp16 autocast with fp32 parameters, forward + loss + "
+                               "backward (tokens uniform from a seed, weights random-init)",
+                   "l2": "activations fit L2; the step is launch- and GEMM-bound at this size"},
+        "attention": {"fwd_ms": a_fwd, "bwd_ms": a_bwd, "fwd_tflops": 4 * dp / (a_fwd / 1e3) / 1e12,
+                      "bwd_tflops": 10 * dp / (a_bwd / 1e3) / 1e12,
+                      "share_of_step": (a_fwd + a_bwd) / ms,
+                      "kernels": "tcgen05 forward / backward at D=64 (fp16)"},
+        "parity": {"max_abs": errs, "tolerance_max_abs": 2e-2,
+                   "pass": errs["out"] <= 2e-2 and all(errs[x] <= 2e-2 * max(1.0, float(r.abs().max()))
+                                                       for x, r in (("dq", rdq), ("dk", rdk), ("dv", rdv))),
+                   "rows": "one attention call at the step's shape, (b,h) = last slice in full"},
+        "roofline": {"bound": "tensor", "kernel": "attention forward + backward at the C2 shape",
+                     "achieved": 14 * dp / ((a_fwd + a_bwd) / 1e3) / 1e12, "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": 14 * dp / ((a_fwd + a_bwd) / 1e3) / 1e12 / peaks["bf16_tflops"],
+                     "peak_source": f"{src} bf16_tflops (dense fp16 = bf16 rate)", "traffic": None,
+                     "algorithmic": f"14*D*causal_pairs over {L} layers = {14 * dp:.4g} FLOP per step"},
+        "gpu_launches": None,
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_c2_attention_baseline(B, H, T, D, L, args.cpu_seconds)
+    return line
+
+
+def cpu_c2_attention_baseline(B, H, T, D, L, budget_s):
+    """The oracle's attention forward + backward (NumPy, fp32 compute of fp16 inputs) at the C2 shape on
+    one (b,h) slice, scaled to the step's B*H slices and L layers."""
+    import numpy as np
+
+    import oracle
+
+    rng = np.random.default_rng(13)
+    q, k, v, g = (rng.standard_normal((1, 1, T, D)).astype(np.float16).astype(np.float32) for _ in range(4))
+    times, start = [], time.perf_counter()
+    while not times or (time.perf_counter() - start < budget_s and len(times) < 50):
+        t0 = time.perf_counter()
+        o, l = oracle.attention_forward(q, k, v, is_causal=True, algorithm="dense")
+        oracle.attention_backward(q, k, v, o, l, g, is_causal=True)
+        times.append(time.perf_counter() - t0)
+    per = statistics.median(times) * B * H * L
+    return {"value": B * T / per, "unit": "tokens/s (attention only)", "cores": cpu_cores(), "kind": "port",
+            "sample": f"oracle fwd+bwd of one (b,h) slice T={T} D={D}, median of {len(times)} reps, scaled x{B * H * L}"}
 
 
 def cpu_c3_baseline(cfg, budget_s):
@@ -813,7 +971,9 @@ def run_c4(args, quantized=False):
                                 else "decode step (kv_append + decode_group + combine)" if Hkv != H
                                 else "decode step (kv_append + decode_split + combine)"),
                      "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"],
-                     "peak_source": f"{src} hbm_gbs", "traffic": None,
+                     "peak_source": f"{src} hbm_gbs",
+                     "traffic": (None if quantized else
+                                 profiled_traffic("c4gqa" if Hkv != H else "c4", kv_bytes / S)),
                      "algorithmic": ("sum_b 2*Hkv*L_b*(D+4) bytes (int8 K+V rows and fp32 scales read) per step"
                                      if quantized else "sum_b 2*Hkv*L_b*D*2 bytes (K+V fp16 read once per KV head) per step")},
         "gpu_launches": S * (2 + (1 if splits else 0)) * args.steps,
@@ -853,10 +1013,10 @@ def main():
         from tensorsmith_b200 import _lib
 
         build = {"lib": str(_lib.LIB_PATH.relative_to(ROOT)), "source_digest": _lib.library_digest()}
-        if args.workload in ("c3", "c5slice", "c4", "c4q", "c4q_small", "c4gqa"):
+        if args.workload in ("c2", "c3", "c5slice", "c4", "c4q", "c4q_small", "c4gqa"):
             if world > 1:
-                raise SystemExit("the c3 / c4 parity configs run on one GPU; c5 is the multi-GPU workload")
-            result = (run_c3(args) if args.workload in ("c3", "c5slice")
+                raise SystemExit("the c2 / c3 / c4 parity configs run on one GPU; c5 is the multi-GPU workload")
+            result = (run_c2(args) if args.workload == "c2" else run_c3(args) if args.workload in ("c3", "c5slice")
                       else run_c4(args, quantized=args.workload.startswith("c4q")))
         else:
             result = run_engine(args, rank, world, local_rank)

@@ -301,10 +301,12 @@ __global__ void __launch_bounds__(384, 1)
         l_run *= factor;
       }
       const float safe = m_run == -INFINITY ? 0.f : m_run;
-      // P = exp2(s * scale * log2e - m) with packed f32x2 arithmetic; every
-      // other element pair goes through MUFU ex2, the rest through the
-      // FMA-pipe polynomial, and bf16 pairs are packed with integer rounding,
-      // so the special function unit stays below the tensor core's time.
+      // P = exp2(s * scale * log2e - m) with packed f32x2 arithmetic; seven
+      // element pairs in eight go through MUFU ex2 and the eighth through the
+      // FMA-pipe polynomial (the split measured fastest at the C5 shape: the
+      // polynomial costs about five times the issue slots of MUFU, and MUFU
+      // alone would take as long as the tile's MMAs), and bf16 pairs are
+      // packed with integer rounding.
       uint32_t pk[kHN / 2];
       uint64_t sum2[2] = {ptx::f2pack(0.f, 0.f), ptx::f2pack(0.f, 0.f)};
       // Dropout (kDrop): keep bits of this half's 64 keys, from the counter-based
@@ -328,7 +330,7 @@ __global__ void __launch_bounds__(384, 1)
         for (int c = 0; c < kHN; c += 2) {
           const uint64_t x2 = ptx::fma2(ptx::f2pack(__uint_as_float(r[c]), __uint_as_float(r[c + 1])), sc2, ng2);
           uint64_t p2;
-          if ((c & 2) == 0) {
+          if ((c & 14) != 14) {
             float x0, x1;
             ptx::f2unpack(x2, x0, x1);
             p2 = ptx::f2pack(ptx::ex2(x0), ptx::ex2(x1));

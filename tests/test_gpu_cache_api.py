@@ -45,7 +45,7 @@ def test_cache_storage_reset_reorder_and_capacity():
 
 def test_cache_requires_inference():
     cache = nn.KVCache(1, 2, 4, 8, device="cuda:0")
-    x = cuda_tensor(np.ones((1, 2, 2, 4), np.float32), requires_scaled=True)
+    x = cuda_tensor(np.ones((1, 2, 2, 4), np.float32), requires_grad=True)
     with pytest.raises(RuntimeError):
         cache.append(x, x)
     with ts.no_grad():
@@ -115,7 +115,7 @@ def test_ragged_cache_append_positions():
 ])
 def test_golden_vjp_fp64(golden, golden_name, kw):
     case = golden(golden_name)
-    tensors = [cuda_tensor(case[n], requires_scaled=True) for n in ("q", "k", "v")]
+    tensors = [cuda_tensor(case[n], requires_grad=True) for n in ("q", "k", "v")]
     out = nn.scaled_dot_product_attention(*tensors, **kw)
     out.backward(cuda_tensor(case["dout"]))
     for name, got in zip(("out", "dq", "dk", "dv"), [out] + [t.grad for t in tensors]):
@@ -125,7 +125,7 @@ def test_golden_vjp_fp64(golden, golden_name, kw):
 @pytest.mark.parametrize("kind", ["bool", "float"])
 def test_golden_masks(golden, kind):
     case = golden("masks")
-    tensors = [cuda_tensor(case[n], requires_scaled=True) for n in ("q", "k", "v")]
+    tensors = [cuda_tensor(case[n], requires_grad=True) for n in ("q", "k", "v")]
     out = nn.scaled_dot_product_attention(*tensors, cuda_tensor(case[f"{kind}_mask"]), is_causal=True)
     out.backward(cuda_tensor(case["dout"]))
     for name, got in zip(("out", "dq", "dk", "dv"), [out] + [t.grad for t in tensors]):
@@ -136,7 +136,7 @@ def test_golden_masks(golden, kind):
 def test_golden_gqa_and_unmasked(golden, tag):
     for name, gqa in (("gqa", True), ("unmasked", False)):
         case = golden(name)
-        tensors = [cuda_tensor(case[n], requires_scaled=True) for n in ("q", "k", "v")]
+        tensors = [cuda_tensor(case[n], requires_grad=True) for n in ("q", "k", "v")]
         out = nn.scaled_dot_product_attention(*tensors, is_causal=tag == "causal", enable_gqa=gqa)
         out.backward(cuda_tensor(case["dout"]))
         for key, got in zip(("out", "dq", "dk", "dv"), [out] + [t.grad for t in tensors]):
@@ -148,7 +148,7 @@ def test_golden_c1_config(golden):
     rng = np.random.default_rng(0)
     raw = [rng.standard_normal((2, 4, 256, 64), dtype=np.float32) for _ in range(3)]
     up = rng.standard_normal((2, 4, 256, 64), dtype=np.float32)
-    tensors = [cuda_tensor(a, requires_scaled=True) for a in raw]
+    tensors = [cuda_tensor(a, requires_grad=True) for a in raw]
     out = nn.scaled_dot_product_attention(*tensors, is_causal=True)
     out.backward(cuda_tensor(up))
     step = int(case["rows_step"])
@@ -158,7 +158,7 @@ def test_golden_c1_config(golden):
 
 def test_golden_half_inputs(golden):
     case = golden("half")
-    tensors = [cuda_tensor(case[n], requires_scaled=True) for n in ("q", "k", "v")]
+    tensors = [cuda_tensor(case[n], requires_grad=True) for n in ("q", "k", "v")]
     out = nn.scaled_dot_product_attention(*tensors, is_causal=True)
     out.backward(cuda_tensor(case["dout"]))
     for key, got in zip(("out", "dq", "dk", "dv"), [out] + [t.grad for t in tensors]):
@@ -167,7 +167,7 @@ def test_golden_half_inputs(golden):
 
 def test_no_grad_returns_plain_tensor_and_permute_vjp():
     rng = np.random.default_rng(4)
-    x = [cuda_tensor(rng.standard_normal((1, 5, 2, 8)).astype(np.float32), requires_scaled=True) for _ in range(3)]
+    x = [cuda_tensor(rng.standard_normal((1, 5, 2, 8)).astype(np.float32), requires_grad=True) for _ in range(3)]
     q, k, v = (t.permute(0, 2, 1, 3) for t in x)
     with ts.no_grad():
         plain = nn.scaled_dot_product_attention(q, k, v, is_causal=True)

@@ -100,7 +100,7 @@ def test_sdpa_dropout_api_and_tape():
     rng = np.random.default_rng(8)
     raw = [rng.normal(size=(1, 2, 6, 8)).astype(np.float32) for _ in range(3)]
     up = rng.normal(size=(1, 2, 6, 8)).astype(np.float32)
-    tensors = [ts.Tensor(torch.from_numpy(a).cuda(), requires_scaled=True) for a in raw]
+    tensors = [ts.Tensor(torch.from_numpy(a).cuda(), requires_grad=True) for a in raw]
     ts.seed(8)
     out = nn.scaled_dot_product_attention(*tensors, dropout_p=0.3, is_causal=True)
     out.backward(ts.Tensor(torch.from_numpy(up).cuda()))
