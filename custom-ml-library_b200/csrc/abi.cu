@@ -112,6 +112,8 @@ const char* ts_attn_strerror(int status) {
 int ts_attn_fwd_path(const ts_attn_params* p, int decode) {
   const int st = check_params(p);
   if (st != TS_OK) return st;
+  ts_attn_params view;
+  if (decode && tsa::gqa_decode_view(*p, &view)) return TS_PATH_TCGEN05;
   if (decode && tsa::decode_supported(*p)) return TS_PATH_DECODE;
   if (tsa::tc_fwd_supported(*p)) return TS_PATH_TCGEN05;
   return TS_PATH_SIMT;
@@ -125,13 +127,18 @@ int ts_attn_fwd(const ts_attn_params* p, void* stream) {
 }
 
 size_t ts_attn_decode_workspace_size(const ts_attn_params* p) {
-  if (check_params(p) != TS_OK || !tsa::decode_supported(*p)) return 0;
+  ts_attn_params view;
+  if (check_params(p) != TS_OK || tsa::gqa_decode_view(*p, &view) || !tsa::decode_supported(*p)) return 0;
   return tsa::decode_workspace(*p);
 }
 
 int ts_attn_decode(const ts_attn_params* p, void* workspace, size_t workspace_bytes, void* stream) {
   const int st = check_params(p);
   if (st != TS_OK) return st;
+  // A grouped-query step over enough (batch, KV head) pairs runs on the
+  // tensor cores, the query heads of each KV head as the rows of one tile.
+  ts_attn_params view;
+  if (tsa::gqa_decode_view(*p, &view)) return from_cuda(tsa::tc_forward(view, fault_ptr(), as_stream(stream)));
   // Problems the split-K kernels do not take (many query rows, explicit masks,
   // value_dim != head_dim) go where ts_attn_fwd would send them; neither path
   // needs a workspace.

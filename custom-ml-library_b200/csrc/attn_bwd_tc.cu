@@ -542,7 +542,7 @@ template <int D, bool BF16>
 static cudaError_t launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                               const CUtensorMap& mdo, const TcBwdArgs& a, cudaStream_t st) {
   auto kern = a.drop.p > 0.f ? tc_bwd_kernel<D, BF16, true> : tc_bwd_kernel<D, BF16, false>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdCfg<D>::kSmem);
+  cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(kern), BwdCfg<D>::kSmem);
   if (e != cudaSuccess) return e;
   dim3 grid(a.n_k_tiles, a.p.kv_heads, a.p.batch);
   kern<<<grid, 384, BwdCfg<D>::kSmem, st>>>(mq, mk, mv, mdo, a);

@@ -484,11 +484,34 @@ bool tc_fwd_supported(const ts_attn_params& p) {
   return encode_fn() != nullptr;
 }
 
+bool gqa_decode_view(const ts_attn_params& p, ts_attn_params* view) {
+  if (p.q_len != 1 || p.mask_kind != TS_MASK_NONE || p.kv_heads <= 0 || p.q_heads % p.kv_heads) return false;
+  const int rep = p.q_heads / p.kv_heads;
+  if (rep < 2 || rep > 128) return false;
+  // The one query must see every valid key (the rows of the view share its position).
+  if (p.is_causal && !p.kv_lens && p.causal_offset + 1 < p.kv_len) return false;
+  if ((int64_t)p.batch * p.kv_heads < kGqaViewMinPairs) return false;
+  ts_attn_params v = p;
+  v.q_heads = p.kv_heads;
+  v.q_len = rep;
+  v.q.stride[1] = p.q.stride[1] * rep;
+  v.q.stride[2] = p.q.stride[1];
+  v.o.stride[1] = p.o.stride[1] * rep;
+  v.o.stride[2] = p.o.stride[1];
+  v.lse_stride[1] = p.lse_stride[1] * rep;
+  v.lse_stride[2] = p.lse_stride[1];
+  v.is_causal = 0;
+  v.causal_offset = 0;
+  if (!tc_fwd_supported(v)) return false;
+  *view = v;
+  return true;
+}
+
 template <int D, bool BF16>
 static cudaError_t launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                              const TcFwdArgs& a, cudaStream_t st) {
   auto kern = a.drop.p > 0.f ? tc_fwd_kernel<D, BF16, true> : tc_fwd_kernel<D, BF16, false>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::kSmem);
+  cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(kern), Cfg<D>::kSmem);
   if (e != cudaSuccess) return e;
   dim3 grid(a.n_q_tiles, a.p.q_heads, a.p.batch);
   kern<<<grid, 384, Cfg<D>::kSmem, st>>>(mq, mk, mv, a);

@@ -9,4 +9,19 @@ bool tc_fwd_supported(const ts_attn_params& p);
 // `drop` set: attention dropout on P before P.V (the generic kernels' mask).
 cudaError_t tc_forward(const ts_attn_params& p, uint32_t* fault, cudaStream_t stream,
                        const DropoutArgs* drop = nullptr);
+
+// Fewest (batch, KV head) pairs for which a grouped-query decode step runs on
+// the prefill kernel (one CTA per pair, no split along the keys): with fewer,
+// the split-K decode keeps more SMs busy.
+constexpr int64_t kGqaViewMinPairs = 64;
+
+// A one-token decode step of a grouped-query problem (2 to 128 query heads per
+// KV head, no explicit mask, the query seeing every valid key) as a prefill
+// problem: the query heads of one KV head become the rows of one query tile,
+// with no causal rule among them (same position) and the same key range and
+// kv_lens.  The tcgen05 kernel then streams each KV head once with its whole
+// group on the tensor cores.  Fills `view` and returns true when the problem
+// qualifies, at least kGqaViewMinPairs pairs run and the tensor-core kernel
+// takes the view.
+bool gqa_decode_view(const ts_attn_params& p, ts_attn_params* view);
 }  // namespace tsa

@@ -50,6 +50,29 @@ inline EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) for `kern` on the current
+// device, called once per (kernel, device): the attribute persists, and small
+// problems (a few microseconds of GPU work) otherwise pay the call every launch.
+inline cudaError_t ensure_max_smem(const void* kern, int bytes) {
+  struct Entry {
+    const void* kern;
+    int device;
+  };
+  constexpr int kEntries = 512;
+  static Entry done[kEntries];
+  static int used = 0;
+  static std::mutex lock;
+  int device = -1;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> guard(lock);
+  for (int i = 0; i < used; ++i)
+    if (done[i].kern == kern && done[i].device == device) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && used < kEntries) done[used++] = Entry{kern, device};
+  return e;
+}
+
 // A 2-byte-element view a TMA map can address: unit channel stride, 16-byte
 // aligned base and strides.
 inline bool view_tma_ok(const ts_view4& v) {

@@ -157,9 +157,13 @@ TS_ATTN_API size_t ts_attn_decode_workspace_size(const ts_attn_params* params);
 
 /* Cached decode: a few query tokens against a long KV cache, split along the
  * keys and combined.  Same semantics as ts_attn_fwd; replaces the cached call
- * of nn/transformer.py:144-154 into nn/attention.py:132-145.  Problems the
- * split-K kernels do not take (ts_attn_fwd_path(params, 1) != TS_PATH_DECODE)
- * run exactly as ts_attn_fwd and need no workspace. */
+ * of nn/transformer.py:144-154 into nn/attention.py:132-145.  A grouped-query
+ * step (one query token, 2-128 query heads per KV head, no mask, at least 64
+ * (batch, KV head) pairs) runs on the tcgen05 prefill kernel with the query
+ * heads of each KV head as the rows of one tile (ts_attn_fwd_path(params, 1)
+ * then returns TS_PATH_TCGEN05).  Problems neither kernel family takes
+ * (ts_attn_fwd_path(params, 1) != TS_PATH_DECODE) run exactly as ts_attn_fwd;
+ * only TS_PATH_DECODE needs a workspace. */
 TS_ATTN_API int ts_attn_decode(const ts_attn_params* params, void* workspace, size_t workspace_bytes,
                    void* stream);
 

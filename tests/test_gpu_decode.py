@@ -75,3 +75,55 @@ def test_decode_strided_cache_view():
     ref, _ = oracle.attention_forward(q, k[:, :, :n], v[:, :, :n], is_causal=True, causal_offset=n - 1,
                                       algorithm="dense")
     assert_close(to_np(out), ref, "bfloat16", "view")
+
+
+# (B, Hq, Hkv, cap, lengths, causal_offset or None): grouped-query steps over >= 64 (batch, KV head) pairs
+GQA_VIEW_CASES = [
+    (16, 32, 4, 1500, "ragged", None),          # rep 8, per-row lengths
+    (32, 16, 8, 700, "ragged", None),           # rep 2
+    (8, 64, 8, 3000, "full", 2999),             # rep 8, scalar offset at the end of the cache
+    (64, 24, 8, 300, "ragged", None),           # rep 3 (rows not a power of two)
+]
+
+
+@pytest.mark.parametrize("name", ["bfloat16", "float16"])
+@pytest.mark.parametrize("case", GQA_VIEW_CASES, ids=str)
+def test_gqa_decode_on_tensor_cores(case, name):
+    """A grouped-query decode step with enough (batch, KV head) pairs runs on the tcgen05 kernel with the
+    query heads of a KV head as the rows of one tile; output and LSE match the oracle."""
+    b, hq, hkv, cap, kind, off = case
+    rng = np.random.default_rng(29)
+    lens = rng.integers(1, cap + 1, b) if kind == "ragged" else np.full(b, cap)
+    q = rounded(rng.standard_normal((b, hq, 1, 128)), name)
+    k = rounded(rng.standard_normal((b, hkv, cap, 128)), name)
+    v = rounded(rng.standard_normal((b, hkv, cap, 128)), name)
+    tq_, tk_, tv_ = (to_cuda(x, name) for x in (q, k, v))
+    if off is None:
+        kw = dict(is_causal=True, kv_lens=torch.tensor(lens, dtype=torch.int32, device="cuda"))
+        ref, ref_lse = oracle.decode_attention(q, k, v, lens, enable_gqa=True)
+    else:
+        kw = dict(is_causal=True, causal_offset=off)
+        ref, ref_lse = oracle.attention_forward(q, k, v, is_causal=True, causal_offset=off, enable_gqa=True,
+                                                algorithm="dense")
+    assert engine.fwd_path(tq_, tk_, tv_, decode=True, **kw) == "tcgen05"
+    assert engine.decode_workspace_bytes(tq_, tk_, tv_, **kw) == 0
+    out, lse = engine.decode(tq_, tk_, tv_, need_lse=True, **kw)
+    torch.cuda.synchronize()
+    engine.check_device_status()
+    assert_close(to_np(out), ref, name, f"gqa view {case}")
+    assert_close(to_np(lse), ref_lse, name, f"gqa view lse {case}")
+
+
+def test_gqa_decode_keeps_split_k_when_the_query_does_not_see_every_key():
+    """A causal offset that hides the end of the cache, or too few pairs, keeps the split-K decode."""
+    rng = np.random.default_rng(31)
+    q = rounded(rng.standard_normal((16, 32, 1, 128)), "bfloat16")
+    k = rounded(rng.standard_normal((16, 4, 800, 128)), "bfloat16")
+    v = rounded(rng.standard_normal((16, 4, 800, 128)), "bfloat16")
+    tq_, tk_, tv_ = (to_cuda(x, "bfloat16") for x in (q, k, v))
+    assert engine.fwd_path(tq_, tk_, tv_, decode=True, is_causal=True, causal_offset=500) == "decode"
+    out, _ = engine.decode(tq_, tk_, tv_, is_causal=True, causal_offset=500)
+    ref, _ = oracle.attention_forward(q, k, v, is_causal=True, causal_offset=500, enable_gqa=True, algorithm="dense")
+    assert_close(to_np(out), ref, "bfloat16", "short offset, grouped")
+    few = [to_cuda(x[:2], "bfloat16") for x in (q, k, v)]  # 8 pairs
+    assert engine.fwd_path(*few, decode=True, is_causal=True, causal_offset=799) == "decode"

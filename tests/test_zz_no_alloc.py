@@ -45,7 +45,7 @@ def _noalloc(q, k, v, kv_lens):
 
 def test_noalloc_decode_matches_workspace_decode_twice():
     problems = [
-        _problem(1, 8, 32, 8, 6000, [6000, 1, 4097, 2500, 33, 5999, 1024, 3000]),
+        _problem(1, 8, 32, 4, 6000, [6000, 1, 4097, 2500, 33, 5999, 1024, 3000]),  # 32 pairs: split-K
         _problem(2, 4, 16, 16, 3000, [7, 3000, 1500, 2049]),
     ]
     for q, k, v, kv_lens in problems:
@@ -79,3 +79,15 @@ def test_noalloc_rejects_problems_larger_than_the_scratch():
     assert status == _lib.ERR_WORKSPACE
     with pytest.raises(_lib.EngineError, match="8 MiB"):
         engine.decode_noalloc(q, k, v, is_causal=True)
+
+
+def test_noalloc_decode_of_a_step_that_needs_no_scratch():
+    # A grouped-query step over 64 (batch, KV head) pairs runs on the tensor-core
+    # prefill kernel, which keeps no partials: the entry point still answers it.
+    q, k, v, kv_lens = _problem(4, 16, 32, 4, 900, list(range(100, 900, 50)))
+    assert engine.decode_workspace_bytes(q, k, v, is_causal=True, kv_lens=kv_lens) == 0
+    ref, _ = engine.decode(q, k, v, is_causal=True, kv_lens=kv_lens)
+    status, out, _ = _noalloc(q, k, v, kv_lens)
+    assert status == _lib.OK, _lib.strerror(status)
+    engine.check_device_status()
+    assert (out.float() - ref.float()).abs().max().item() <= HALF_MAXABS
