@@ -61,6 +61,11 @@ WORKLOADS = {
 }
 # Query rows per prefill chunk when N > 1 (each chunk's output gather overlaps the next chunk).
 PREFILL_CHUNK_ROWS = 4096
+# CTAs the overlapped prefill gathers may use (NCCL config max_ctas of their own process group):
+# NCCL's blocks take whole SMs from the compute-bound forward while they run.  Measured on 2 B200s
+# (prefill ms = forward + gather tail): NCCL's default 164.2 + 0.6, a cap of 2 152.4 + 25.4, 4
+# 153.2 + 10.6, 8 155.1 + 4.1, 16 157.7 + 2.1; one gather after an unchunked forward 151.0 + 6.2.
+PREFILL_GATHER_CTAS = 8
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the scored kernel, from the ncu
 # captures summarised under profiles/, per unit of work so a launch of any size scales by its units.
@@ -407,10 +412,16 @@ def run_engine(args, rank: int, world: int, local_rank: int):
         if world > 1:
             gather_to_root(src, plan, out=dst)
 
-    def gather_async(src, full):
+    def gather_async(src, full, group=None):
         # full: [world, ...] on rank 0; rank r's shard lands in full[r:r+1]
         targets = None if full is None else [full[r : r + 1] for r in range(world)]
-        return gather_to_root(src, plan, out=targets, async_op=True)
+        return gather_to_root(src, plan, out=targets, async_op=True, group=group)
+
+    prefill_group = None
+    if world > 1:
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.config.max_ctas = PREFILL_GATHER_CTAS
+        prefill_group = dist.new_group(list(range(world)), pg_options=opts)
 
     def step(ev):
         ev[0].record()
@@ -421,7 +432,8 @@ def run_engine(args, rank: int, world: int, local_rank: int):
             for c, (r0, r1) in enumerate(chunks):
                 engine.forward(q[:, :, r0:r1], kc[:, :, :r1], vc[:, :, :r1], is_causal=True, causal_offset=r0,
                                need_lse=False, out=o_parts[c])
-                works.append(gather_async(o_parts[c], None if o_full_parts is None else o_full_parts[c]))
+                works.append(gather_async(o_parts[c], None if o_full_parts is None else o_full_parts[c],
+                                          prefill_group))
         ev[1].record()
         for work in works:
             work.wait()
@@ -508,7 +520,8 @@ def run_engine(args, rank: int, world: int, local_rank: int):
                              f"steps (KV append + split-K decode), (b,h) pairs sharded over {world} GPU(s), "
                              "outputs gathered to rank 0 over NCCL (with N > 1 the prefill runs in "
                              f"{len(chunks)} query-row chunks, longest first, each chunk's gather overlapping the "
-                             "next chunk; decode gathers queued and waited for at the end of the step)"),
+                             f"next chunk on a process group held to {PREFILL_GATHER_CTAS} NCCL CTAs; decode "
+                             "gathers queued and waited for at the end of the step)"),
                 "global_batch": B, "seq_len": T, "parallelism": f"bxh-shard{world}",
                 "l2": "inputs larger than L2 (Q/K/V/cache >= 8 GB per step)",
             },
