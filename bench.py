@@ -582,14 +582,20 @@ def run_e2e(args, cfg, plan, rank, world, local_rank, q, kc, vc, qd, kd, vd, ws,
     dod = torch.empty_like(qd)
     od_full = torch.empty(S, world, n, 1, D, dtype=q.dtype, device=dev) if rank == 0 and world > 1 else None
 
-    # Prefill inputs stream in on their own stream, chunk by chunk of (b,h) pairs, so the
-    # host-to-device copy of chunk c+1 overlaps the forward of chunk c; the output's
-    # device-to-host copy overlaps the decode loop.  The step still ends only when every
-    # copy has landed.
+    # (b,h) pairs are independent through prefill and decode, so the step runs chunk by chunk of
+    # pairs: chunk c's inputs land on a copy stream while chunk c-1 computes, then chunk c's
+    # prefill and its S decode steps run, and its prefill output goes back to the host on a
+    # second copy stream while chunk c+1 computes.  The decode inputs of every step (small) land
+    # first, the decode outputs go back at the end.  With N > 1 every rank's outputs are gathered
+    # to rank 0 after the last chunk and copied back from there.  The step ends when every copy
+    # has landed.
     n_chunks = max(1, min(8, n))
     bounds = [round(i * n / n_chunks) for i in range(n_chunks + 1)]
     compute = torch.cuda.current_stream(dev)
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    dkd, dvd = torch.empty_like(kd), torch.empty_like(vd)
+    od_all = torch.empty((world * S,) + tuple(qd.shape[1:]), dtype=q.dtype, device=dev) if rank == 0 and world > 1 else None
+    ho_v = ho.view(1, n, T, D) if world == 1 else None
 
     def step():
         start = compute.record_event()
@@ -598,6 +604,8 @@ def run_e2e(args, cfg, plan, rank, world, local_rank, q, kc, vc, qd, kd, vd, ws,
         landed = []
         with torch.cuda.stream(s_in):
             dqd.copy_(hqd, non_blocking=True)
+            dkd.copy_(hkd, non_blocking=True)
+            dvd.copy_(hvd, non_blocking=True)
             for c in range(n_chunks):
                 c0, c1 = bounds[c], bounds[c + 1]
                 dq[:, c0:c1].copy_(hq[:, c0:c1], non_blocking=True)
@@ -609,21 +617,23 @@ def run_e2e(args, cfg, plan, rank, world, local_rank, q, kc, vc, qd, kd, vd, ws,
             compute.wait_event(landed[c])
             engine.forward(dq[:, c0:c1], kc[:, c0:c1, :T], vc[:, c0:c1, :T], is_causal=True, need_lse=False,
                            out=do[:, c0:c1])
-        gather(do, o_full)
+            if ho_v is not None:
+                s_out.wait_event(compute.record_event())
+                with torch.cuda.stream(s_out):
+                    ho_v[:, c0:c1].copy_(do[:, c0:c1], non_blocking=True)
+            for s in range(S):
+                engine.kv_append(dkd[s][:, c0:c1], dvd[s][:, c0:c1], kc[:, c0:c1], vc[:, c0:c1], position=T + s)
+                engine.decode(dqd[s][:, c0:c1], kc[:, c0:c1, : T + s + 1], vc[:, c0:c1, : T + s + 1], is_causal=True,
+                              causal_offset=T + s, out=dod[s][:, c0:c1], workspace=ws)
+        if world > 1:
+            gather(do, o_full)
+            gather(dod, od_all)
         if rank == 0:
             s_out.wait_event(compute.record_event())
             with torch.cuda.stream(s_out):
-                ho.view(-1).copy_((o_full if o_full is not None else do).view(-1), non_blocking=True)
-        for s in range(S):
-            kd_s = hkd[s].to(dev, non_blocking=True)
-            vd_s = hvd[s].to(dev, non_blocking=True)
-            engine.kv_append(kd_s, vd_s, kc, vc, position=T + s)
-            engine.decode(dqd[s], kc[:, :, : T + s + 1], vc[:, :, : T + s + 1], is_causal=True,
-                          causal_offset=T + s, out=dod[s], workspace=ws)
-            gather(dod[s], None if od_full is None else od_full[s])
-            if rank == 0:
-                hod[s].copy_((od_full[s] if od_full is not None else dod[s]).view(hod[s].shape),
-                             non_blocking=True)
+                if world > 1:
+                    ho.view(-1).copy_(o_full.view(-1), non_blocking=True)
+                hod.view(-1).copy_((od_all if od_all is not None else dod).view(-1), non_blocking=True)
         compute.wait_event(s_out.record_event())
 
     steps = max(1, args.steps)
@@ -651,9 +661,10 @@ def run_e2e(args, cfg, plan, rank, world, local_rank, q, kc, vc, qd, kd, vd, ws,
             "ms_per_step_min": ms_min, "ms_per_step_max": ms_max,
             "value_min": flops / (ms_max / 1e3) / 1e12, "value_max": flops / (ms_min / 1e3) / 1e12,
             "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h, "steps": steps,
-            "path": "tensorsmith_b200.engine (C ABI) with pinned host inputs/outputs; prefill inputs "
-                    f"copied in {n_chunks} (b,h) chunks on a copy stream overlapping the forward of the "
-                    "previous chunk, output copied back during the decode loop"}
+            "path": "tensorsmith_b200.engine (C ABI) with pinned host inputs/outputs; the step runs in "
+                    f"{n_chunks} chunks of (b,h) pairs: a chunk's inputs are copied in on a copy stream while "
+                    "the previous chunk's prefill and decode steps run, and its prefill output is copied back "
+                    "while the next chunk runs"}
 
 
 def _timed(args, step, n_events):
