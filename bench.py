@@ -77,8 +77,9 @@ PROFILED_TRAFFIC = {
     "c3": dict(bytes_per_unit=1302.7e6, unit="C3 backward launch", source="profiles/tc_bwd_kernel_c3.md"),
     # split-K decode: DRAM bytes / algorithmic K+V bytes = (268.6 + 4.1) / 268.5
     "c4": dict(bytes_per_unit=1.0156, unit="algorithmic K+V byte", source="profiles/decode_split_kernel_small.md"),
-    # grouped decode: (1348.6 + 8.1) / 1340 (algorithmic K+V bytes of that step)
-    "c4gqa": dict(bytes_per_unit=1.0125, unit="algorithmic K+V byte", source="profiles/decode_group_kernel_c4gqa.md"),
+    # grouped decode on the tcgen05 kernel: (1363.9 + 4.6) / 1345.5 (algorithmic K+V bytes of that step)
+    "c4gqa": dict(bytes_per_unit=1.0171, unit="algorithmic K+V byte",
+                  source="profiles/tc_fwd_kernel_gqa_decode_c4gqa.md"),
 }
 
 
@@ -992,7 +993,7 @@ def run_c4(args, quantized=False):
                    "frac_of_measured_hbm": gbs / peaks["hbm_gbs"], "frac_of_nominal_8000": gbs / 8000.0},
         "roofline": {"bound": "hbm",
                      "kernel": ("decode step (kv_append_int8 + decode_int8 + combine)" if quantized
-                                else "decode step (kv_append + decode_group + combine)" if Hkv != H
+                                else "decode step (kv_append + tc_fwd_kernel over query-head rows)" if Hkv != H
                                 else "decode step (kv_append + decode_split + combine)"),
                      "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"],
                      "peak_source": f"{src} hbm_gbs",
