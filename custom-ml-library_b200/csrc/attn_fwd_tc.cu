@@ -305,8 +305,8 @@ __global__ void __launch_bounds__(384, 1)
       // element pairs in eight go through MUFU ex2 and the eighth through the
       // FMA-pipe polynomial (the split measured fastest at the C5 shape: the
       // polynomial costs about five times the issue slots of MUFU, and MUFU
-      // alone would take as long as the tile's MMAs), and bf16 pairs are
-      // packed with integer rounding.
+      // alone would take as long as the tile's MMAs); pairs are packed with
+      // cvt.rn (measured 1.4 % faster than integer rounding at that shape).
       uint32_t pk[kHN / 2];
       uint64_t sum2[2] = {ptx::f2pack(0.f, 0.f), ptx::f2pack(0.f, 0.f)};
       // Dropout (kDrop): keep bits of this half's 64 keys, from the counter-based
@@ -342,7 +342,7 @@ __global__ void __launch_bounds__(384, 1)
           ptx::f2unpack(p2, p0, p1);
           p0 = dropped(p0, c);
           p1 = dropped(p1, c + 1);
-          pk[c / 2] = kBF16 ? ptx::pack_bf16_rhu(p0, p1) : ptx::pack_f16(p0, p1);
+          pk[c / 2] = kBF16 ? ptx::pack_bf16(p0, p1) : ptx::pack_f16(p0, p1);
         }
       } else {
 #pragma unroll
