@@ -128,6 +128,8 @@ TC_CASES = [
     ("bfloat16", 1, 4, 2, 200, 331, 64, True, 131, 0.2),
     ("bfloat16", 2, 2, 2, 130, 130, 128, False, 0, 0.5),
     ("float16", 1, 2, 1, 257, 257, 128, True, 0, 0.1),
+    # 148 pairs x 2 units: the persistent forward's kDrop instantiation
+    ("bfloat16", 1, 148, 74, 300, 300, 64, True, 0, 0.2),
 ]
 
 

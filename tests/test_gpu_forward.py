@@ -83,6 +83,49 @@ def test_forward_tcgen05(shape, name):
     assert engine.fwd_path(q, k, v, is_causal=causal, causal_offset=off) == "tcgen05"
 
 
+# Causal shapes with at least two work units per SM (a unit = query tiles
+# X-1-t and t of one (batch, head); X query tiles of 128 rows): the forward
+# runs them on the persistent tcgen05 kernel.
+PERSISTENT_SHAPES = [
+    (4, 20, 20, 1024, 1024, 128, 128, True, 0),   # 8 query tiles, 320 units
+    (8, 24, 8, 640, 640, 64, 64, True, 0),        # 5 tiles: the middle one is a unit alone; GQA
+    (3, 64, 32, 300, 429, 128, 128, True, 129),   # offset, ragged last tile, GQA
+    (160, 2, 1, 129, 129, 64, 64, True, 0),       # second tile holds one row
+    (1, 300, 300, 100, 100, 64, 64, True, 0),     # one tile per (batch, head)
+    (1, 20, 20, 4096, 4096, 64, 64, True, 0),     # 32 query tiles, the most the schedule takes
+]
+
+
+def _persistent_units(shape):
+    b, hq, _, tq = shape[:4]
+    x = -(-tq // 128)
+    return b * hq * ((x + 1) // 2), x
+
+
+@pytest.mark.parametrize("name", ["bfloat16", "float16"])
+@pytest.mark.parametrize("shape", PERSISTENT_SHAPES, ids=str)
+def test_forward_tcgen05_persistent(shape, name):
+    """Parity of the persistent schedule; the oracle runs one head at a time
+    so that the largest shape stays within a few hundred MB on the host."""
+    b, hq, hkv, tq, tk, d, dv, causal, off = shape
+    units, x = _persistent_units(shape)
+    assert x <= 32 and units >= 2 * torch.cuda.get_device_properties(0).multi_processor_count
+    q, k, v = _inputs(shape, name, 5)
+    tq_, tk_, tv_ = (to_cuda(a, name) for a in (q, k, v))
+    assert engine.fwd_path(tq_, tk_, tv_, is_causal=True, causal_offset=off) == "tcgen05"
+    out, lse = engine.forward(tq_, tk_, tv_, is_causal=True, causal_offset=off)
+    torch.cuda.synchronize()
+    engine.check_device_status()
+    out, lse = to_np(out), to_np(lse)
+    rep = hq // hkv
+    for h in range(hq):
+        sl = slice(h, h + 1)
+        kv = slice(h // rep, h // rep + 1)
+        ref_o, ref_lse = oracle_forward(q[:, sl], k[:, kv], v[:, kv], is_causal=True, causal_offset=off)
+        assert_close(out[:, sl], ref_o, name, f"out {shape} head {h}")
+        np.testing.assert_allclose(lse[:, sl], ref_lse, rtol=2e-3, atol=2e-3)
+
+
 def test_negative_scale_routes_to_generic_path():
     rng = np.random.default_rng(8)
     q, k, v = (rounded(rng.standard_normal((1, 2, 130, 64)), "bfloat16") for _ in range(3))
