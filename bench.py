@@ -105,6 +105,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
+    ap.add_argument("--dropout", type=float, default=0.0,
+                    help="c3: attention dropout probability in the timed forward and backward")
     ap.add_argument("--clock-log", default=None,
                     help="file for the nvidia-smi clock samples of the timed region (default: a temp file)")
     return ap.parse_args()
@@ -144,8 +146,10 @@ def ref_rows(q_rows, k, v, limits, scale):
     return (e @ v.double()) / l, (m + torch.log(l))[:, 0]
 
 
-def ref_slice_backward(q, k, v, do, scale):
-    """fp64 causal attention of one (b, h) slice and its VJP: (o, lse, dq, dk, dv)."""
+def ref_slice_backward(q, k, v, do, scale, keep=None, drop_p=0.0):
+    """fp64 causal attention of one (b, h) slice and its VJP: (o, lse, dq, dk, dv).  With a
+    keep mask [T, T] the probabilities are scaled by keep / (1 - drop_p) before P.V and dP by
+    the same factor, as the reference's dense dropout (nn/attention.py:140-144, 212-216)."""
     import torch
 
     q, k, v, do = (x.double() for x in (q, k, v, do))
@@ -154,9 +158,13 @@ def ref_slice_backward(q, k, v, do, scale):
     s = s.masked_fill(torch.ones(t, t, dtype=torch.bool).triu(1), float("-inf"))
     lse = torch.logsumexp(s, dim=1)
     p = torch.exp(s - lse[:, None])
-    o = p @ v
-    dv = p.T @ do
+    f = None if keep is None else keep.double() / (1.0 - drop_p)
+    pd = p if f is None else p * f
+    o = pd @ v
+    dv = pd.T @ do
     dp = do @ v.T
+    if f is not None:
+        dp = dp * f
     ds = p * (dp - (do * o).sum(dim=1, keepdim=True)) * scale
     return o, lse, ds @ k, ds.T @ q, dv
 
@@ -711,11 +719,15 @@ def run_c3(args):
     lse = torch.empty(B, H, T, dtype=torch.float32, device=dev)
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
 
+    if args.dropout > 0 and T > 8192:
+        raise SystemExit("--dropout: the parity check holds the slice's mask in full, so T <= 8192 (c3)")
+    drop = (args.dropout, 1234, 0) if args.dropout > 0 else None
+
     def step(ev):
         ev[0].record()
-        engine.forward(q, k, v, is_causal=True, out=out, lse=lse)
+        engine.forward(q, k, v, is_causal=True, out=out, lse=lse, dropout=drop)
         ev[1].record()
-        engine.backward(q, k, v, out, lse, do, is_causal=True, dq=dq, dk=dk, dv=dv)
+        engine.backward(q, k, v, out, lse, do, is_causal=True, dq=dq, dk=dk, dv=dv, dropout=drop)
         ev[2].record()
 
     evs, step_ms, clocks = _timed(args, step, 3)
@@ -730,8 +742,11 @@ def run_c3(args):
     # gradients), or at T = 32768 the forward on 256 sampled rows of it
     bs, hs = B - 1, H - 1
     if T <= 8192:
+        keep = None
+        if drop is not None:  # the kernels' own mask, materialised for this slice only
+            keep = engine.dropout_mask(B, H, T, T, drop, dev)[bs, hs].cpu()
         ro, rl, rdq, rdk, rdv = ref_slice_backward(q[bs, hs].cpu(), k[bs, hs].cpu(), v[bs, hs].cpu(),
-                                                   do[bs, hs].cpu(), D ** -0.5)
+                                                   do[bs, hs].cpu(), D ** -0.5, keep, args.dropout)
         errs = {"out": max_abs(out[bs, hs], ro), "lse": max_abs(lse[bs, hs], rl), "dq": max_abs(dq[bs, hs], rdq),
                 "dk": max_abs(dk[bs, hs], rdk), "dv": max_abs(dv[bs, hs], rdv)}
         peaks_ref = {"dq": float(rdq.abs().max()), "dk": float(rdk.abs().max()), "dv": float(rdv.abs().max())}
@@ -752,7 +767,8 @@ def run_c3(args):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"{args.workload}: causal attention bf16 B={B} H={H} T={T} D={D}, forward + "
                                "backward, Q/K/V ~ N(0,1)" + ("/sqrt(128)" if in_scale != 1.0 else "")
-                               + ", dO ~ N(0,1)",
+                               + ", dO ~ N(0,1)"
+                               + (f", attention dropout p={args.dropout} (in-kernel Philox mask)" if drop else ""),
                    "l2": f"inputs larger than L2 ({5 * B * H * T * D * 2 / 1e9:.2f} GB per step)"},
         "parity": parity,
         "forward": {"tflops": fwd_tf, "ms": fwd, "frac_of_measured_bf16": fwd_tf / peaks["bf16_tflops"]},

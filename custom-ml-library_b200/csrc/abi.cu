@@ -1,5 +1,6 @@
 // extern "C" entry points of libts_attn.so (declared in include/ts_attn.h):
 // argument validation, kernel selection and the device fault word.
+#include <cmath>
 #include <cstdio>
 #include <mutex>
 
@@ -225,6 +226,7 @@ namespace {
 bool make_dropout(const ts_dropout* d, tsa::DropoutArgs& out) {
   if (!d || !(d->p >= 0.0) || !(d->p < 1.0)) return false;
   out.p = (float)d->p;
+  out.keep_min = (uint32_t)std::ceil(d->p * 65536.0);
   out.inv_keep_f = 1.0f / (float)(1.0 - d->p);
   out.inv_keep_d = 1.0 / (1.0 - d->p);
   out.seed = d->seed;

@@ -289,20 +289,20 @@ __global__ void __launch_bounds__(384, 1)
             nd2[c / 2] = ptx::f2pack(d4.x, d4.y), nd2[c / 2 + 1] = ptx::f2pack(d4.z, d4.w);
           }
           // Dropout (kDrop): keep bit of (this key, column 32*half + c) in bit c.  The
-          // generator gives the bits of 4 consecutive keys per call, so the 4 lanes
-          // of a key quad each draw one column of every 4 and swap nibbles.
+          // generator gives the bits of 8 consecutive keys per call, so the 8 lanes
+          // of a key octet each draw one column of every 8 and swap bytes.
           uint32_t kb = 0xffffffffu;
           if constexpr (kDrop) {
             kb = 0u;
             const uint32_t bh = (uint32_t)(b * p.q_heads + it_head(it));
-            const uint32_t j4 = (uint32_t)key >> 2;
-            const int quad = lane & ~3, sub = lane & 3;
+            const uint32_t j8 = (uint32_t)key >> 3;
+            const int oct = lane & ~7, sub = lane & 7;
 #pragma unroll
-            for (int g = 0; g < 8; ++g) {
-              const uint32_t nib = dropout_keep4(args.drop, bh, (uint32_t)(q0 + 32 * half + 4 * g + sub), j4);
+            for (int g = 0; g < 4; ++g) {
+              const uint32_t byte = dropout_keep8(args.drop, bh, (uint32_t)(q0 + 32 * half + 8 * g + sub), j8);
 #pragma unroll
-              for (int t = 0; t < 4; ++t)
-                kb |= ((__shfl_sync(0xffffffffu, nib, quad + t) >> sub) & 1u) << (4 * g + t);
+              for (int t = 0; t < 8; ++t)
+                kb |= ((__shfl_sync(0xffffffffu, byte, oct + t) >> sub) & 1u) << (8 * g + t);
             }
           }
           const float dinv = kDrop ? args.drop.inv_keep_f : 1.f;

@@ -338,8 +338,8 @@ __global__ void __launch_bounds__(384, 1)
         const uint32_t bh = (uint32_t)(b * p.q_heads + h);
         keep[0] = keep[1] = 0u;
 #pragma unroll
-        for (int j4 = 0; j4 < kHN / 4; ++j4)
-          keep[j4 >> 3] |= dropout_keep4(args.drop, bh, (uint32_t)qi, (uint32_t)(k0 / 4 + j4)) << (4 * (j4 & 7));
+        for (int j8 = 0; j8 < kHN / 8; ++j8)
+          keep[j8 >> 2] |= dropout_keep8(args.drop, bh, (uint32_t)qi, (uint32_t)(k0 / 8 + j8)) << (8 * (j8 & 3));
       }
       auto dropped = [&](float pv, int c) -> float {
         if constexpr (kDrop) return (keep[c >> 5] >> (c & 31)) & 1u ? pv * args.drop.inv_keep_f : 0.f;
@@ -806,8 +806,8 @@ __global__ void __launch_bounds__(384, 1)
             const uint32_t bh = (uint32_t)(b * p.q_heads + h);
             keep[0] = keep[1] = 0u;
     #pragma unroll
-            for (int j4 = 0; j4 < kHN / 4; ++j4)
-              keep[j4 >> 3] |= dropout_keep4(args.drop, bh, (uint32_t)qi, (uint32_t)(k0 / 4 + j4)) << (4 * (j4 & 7));
+            for (int j8 = 0; j8 < kHN / 8; ++j8)
+              keep[j8 >> 2] |= dropout_keep8(args.drop, bh, (uint32_t)qi, (uint32_t)(k0 / 8 + j8)) << (8 * (j8 & 3));
           }
           auto dropped = [&](float pv, int c) -> float {
             if constexpr (kDrop) return (keep[c >> 5] >> (c & 31)) & 1u ? pv * args.drop.inv_keep_f : 0.f;

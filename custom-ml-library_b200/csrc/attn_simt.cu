@@ -51,14 +51,14 @@ cudaError_t simt_backward(const ts_attn_bwd_params& bp, void* ws, cudaStream_t s
   return cudaErrorInvalidValue;
 }
 
-// One CTA per (query row, head, batch row); threads over keys in groups of 4.
+// One CTA per (query row, head, batch row); threads over keys in groups of 8.
 __global__ void dropout_mask_kernel(DropoutArgs d, int heads, int q_len, int kv_len, uint8_t* mask) {
   const int i = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const uint32_t bh = (uint32_t)(b * heads + h);
   uint8_t* row = mask + (((int64_t)b * heads + h) * q_len + i) * kv_len;
-  for (int j4 = threadIdx.x; j4 * 4 < kv_len; j4 += blockDim.x) {
-    const uint32_t bits = dropout_keep4(d, bh, (uint32_t)i, (uint32_t)j4);
-    for (int k = 0; k < 4 && j4 * 4 + k < kv_len; ++k) row[j4 * 4 + k] = (bits >> k) & 1u;
+  for (int j8 = threadIdx.x; j8 * 8 < kv_len; j8 += blockDim.x) {
+    const uint32_t bits = dropout_keep8(d, bh, (uint32_t)i, (uint32_t)j8);
+    for (int k = 0; k < 8 && j8 * 8 + k < kv_len; ++k) row[j8 * 8 + k] = (bits >> k) & 1u;
   }
 }
 

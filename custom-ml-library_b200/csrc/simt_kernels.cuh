@@ -158,8 +158,8 @@ __global__ void __launch_bounds__(kSimtThreads) simt_fwd_kernel(ts_attn_params p
       keep = 0;
       const uint32_t bh = (uint32_t)(b * p.q_heads + h);
 #pragma unroll
-      for (int j4 = 0; j4 < kSimtKeys / 4; ++j4)
-        keep |= dropout_keep4(drop, bh, (uint32_t)i, (uint32_t)(k0 / 4 + j4)) << (4 * j4);
+      for (int j8 = 0; j8 < kSimtKeys / 8; ++j8)
+        keep |= dropout_keep8(drop, bh, (uint32_t)i, (uint32_t)(k0 / 8 + j8)) << (8 * j8);
     }
 #pragma unroll
     for (int jj = 0; jj < kSimtKeys; ++jj) {
@@ -262,8 +262,8 @@ __global__ void __launch_bounds__(kSimtThreads)
       keep = 0;
       const uint32_t bh = (uint32_t)(b * p.q_heads + h);
 #pragma unroll
-      for (int j4 = 0; j4 < kSimtKeys / 4; ++j4)
-        keep |= dropout_keep4(drop, bh, (uint32_t)i, (uint32_t)(k0 / 4 + j4)) << (4 * j4);
+      for (int j8 = 0; j8 < kSimtKeys / 8; ++j8)
+        keep |= dropout_keep8(drop, bh, (uint32_t)i, (uint32_t)(k0 / 8 + j8)) << (8 * j8);
     }
 #pragma unroll 4
     for (int jj = 0; jj < kSimtKeys; ++jj) {

@@ -207,11 +207,12 @@ TS_ATTN_API int ts_kv_reorder(ts_view4 src, ts_view4 dst, int32_t dtype, int32_t
 TS_ATTN_API int ts_attn_decode_noalloc(const ts_attn_params* params, void* stream);
 
 /* Attention dropout of nn/attention.py:140-144 (forward) and :212-216
- * (backward): P.V uses p * keep / (1 - p) with keep = (u >= p), u uniform in
- * [0, 1) per (batch, query head, query row, key); dP is multiplied by the same
- * factor; LSE stays the softmax normaliser.  u comes from a counter-based
- * generator (Philox4x32-10) keyed by (seed, offset), so a backward given the
- * forward's (seed, offset) regenerates its mask without storing it. */
+ * (backward): P.V uses p * keep / (1 - p) with keep = (u >= p), u uniform on
+ * the 2^16 points k * 2^-16 of [0, 1) per (batch, query head, query row, key);
+ * dP is multiplied by the same factor; LSE stays the softmax normaliser.  u
+ * comes from a counter-based generator (Philox4x32-10, 16 bits per key) keyed
+ * by (seed, offset), so a backward given the forward's (seed, offset)
+ * regenerates its mask without storing it. */
 typedef struct ts_dropout {
   double p;        /* drop probability, 0 <= p < 1 */
   uint64_t seed;   /* generator key */

@@ -29,3 +29,16 @@ def test_ref_slice_backward_matches_oracle():
     rdq, rdk, rdv = oracle.attention_backward(q, k, v, ref_o, ref_l, g, is_causal=True, scale=0.25)
     for got, ref in ((o, ref_o), (l, ref_l), (dq, rdq), (dk, rdk), (dv, rdv)):
         np.testing.assert_allclose(got.numpy(), ref[0, 0], rtol=1e-10, atol=1e-12)
+
+
+def test_ref_slice_backward_with_dropout_matches_oracle():
+    rng = np.random.default_rng(5)
+    q, k, v, g = (rng.standard_normal((1, 1, 29, 16)) for _ in range(4))
+    keep = rng.random((1, 1, 29, 29)) >= 0.3
+    o, l, dq, dk, dv = bench.ref_slice_backward(*(torch.from_numpy(x[0, 0]) for x in (q, k, v, g)), 0.25,
+                                                torch.from_numpy(keep[0, 0]), 0.3)
+    kw = dict(is_causal=True, scale=0.25, dropout_keep=keep, dropout_p=0.3)
+    ref_o, ref_l = oracle.attention_forward(q, k, v, algorithm="dense", **kw)
+    rdq, rdk, rdv = oracle.attention_backward_dense(q, k, v, g, None, **kw)
+    for got, ref in ((o, ref_o), (l, ref_l), (dq, rdq), (dk, rdk), (dv, rdv)):
+        np.testing.assert_allclose(got.numpy(), ref[0, 0], rtol=1e-10, atol=1e-12)
