@@ -73,8 +73,8 @@ PROFILED_TRAFFIC = {
     # tc_fwd_kernel<128,bf16> at T=32768, 8 (b,h) pairs: (201.4 + 51.3) MB / 8 pairs
     "c5": dict(bytes_per_unit=31.59e6, unit="(b,h) pair at T=32768",
                source="profiles/tc_fwd_bwd_kernels_c5slice.md"),
-    # tc_bwd_kernel<128,bf16> at the C3 shape: 809.7 MB read + 493.0 MB written per launch
-    "c3": dict(bytes_per_unit=1302.7e6, unit="C3 backward launch", source="profiles/tc_bwd_kernel_c3.md"),
+    # tc_bwd_kernel<128,bf16> at the C3 shape: 809.6 MB read + 494.3 MB written per launch
+    "c3": dict(bytes_per_unit=1303.9e6, unit="C3 backward launch", source="profiles/tc_bwd_kernel_c3.md"),
     # split-K decode: DRAM bytes / algorithmic K+V bytes = (268.6 + 4.1) / 268.5
     "c4": dict(bytes_per_unit=1.0156, unit="algorithmic K+V byte", source="profiles/decode_split_kernel_small.md"),
     # grouped decode on the tcgen05 kernel: (1363.9 + 4.6) / 1345.5 (algorithmic K+V bytes of that step)

@@ -15,20 +15,29 @@
 //   dV  += P^T dO     [128 x Dv]   A = P^T (TMEM)           B = dO  (MN-major)
 //   dK  += dS^T Q     [128 x D]    A = dS^T(TMEM)           B = Q   (MN-major)
 //   dQ^T = K^T dS^T   [D x 64]     A = K   (smem, MN-major) B = dS^T(smem, MN-major)
-// The "softmax" warpgroup (thread = key row) forms P^T and dS^T from S^T, dP^T
-// and the tile's row statistics, and writes them as bf16/f16 pairs into TMEM
+// Two "softmax" warpgroups (thread = key row) form P^T and dS^T from S^T, dP^T
+// and the tile's row statistics, one over query columns [0, 32) of every
+// tile and one over [32, 64), and write them as bf16/f16 pairs into TMEM
 // (A operands of dV / dK) and dS^T also into a 128-byte-swizzled shared tile
 // (B operand of dQ^T).  Row statistics (-LSE*log2e, -delta, padded to the
 // 64-row tile) are written by a small preprocess kernel and copied by the
 // producer beside each Q/dO tile (3-stage ring).  dQ^T is read by the epilogue
-// warpgroup (thread = channel), staged row-major in shared memory and added
-// into an fp32 dQ accumulator with one bulk reduce-add (cp.reduce.async.bulk
-// .add.f32) per query tile; a final kernel converts it.  dK/dV stay in TMEM
-// for the whole CTA (no atomics, GQA summed).
+// warpgroup (thread = channel), staged channel-major in shared memory with
+// 128-bit stores and added into a tile-major fp32 dQ accumulator with one bulk
+// reduce-add (cp.reduce.async.bulk .add.f32) per query tile; a final kernel
+// transposes and converts it.  dK/dV stay in TMEM for the whole CTA (no
+// atomics, GQA summed).
 //
-// Warps: 0 TMA producer, 1 MMA issuer, 2 TMEM allocator, 4-7 softmax
-// (P^T, dS^T, then the dK/dV epilogue), 8-11 dQ epilogue.  No TMA load uses
-// cluster multicast.
+// Warps: 0 TMA producer, 1 MMA issuer, 2 TMEM allocator, 4-7 and 12-15
+// softmax (P^T, dS^T of their column half, then the dK resp. dV epilogue),
+// 8-11 dQ epilogue.  No TMA load uses cluster multicast.
+//
+// Measured against the one-warpgroup softmax with row-major dQ staging (C3,
+// bf16, D=128): splitting the columns over two warpgroups 531 -> 567 TFLOP/s,
+// and channel-major staging with 128-bit stores (16 stores per thread instead
+// of 64 scalar ones) 567 -> 659.  Double-buffering the staging (which needs a
+// 2-stage Q/dO ring to fit in shared memory) and per-warp 4 KB reduces were
+// slower at T = 32768.
 #include <type_traits>
 
 #include "ptx.cuh"
@@ -53,11 +62,11 @@ template <int D> struct BwdCfg {
   static constexpr int kOffV = kOffK + kSlabs * kKSlab;
   static constexpr int kOffQ = kOffV + kSlabs * kKSlab;                // kQStages stages
   static constexpr int kOffDO = kOffQ + kQStages * kSlabs * kQSlab;     // kQStages stages
-  static constexpr int kOffP = kOffDO + kQStages * kSlabs * kQSlab;
-  static constexpr int kOffDS = kOffP + kKSlab;
+  static constexpr int kOffDS = kOffDO + kQStages * kSlabs * kQSlab;
   static constexpr int kOffStat = kOffDS + kKSlab;             // [stage][-LSE*log2e | -delta][64] floats
-  static constexpr int kOffDQ = kOffStat + kQStages * 2 * kBM * 4;  // [64][D] fp32 dQ staging
-  static constexpr int kOffBar = kOffDQ + kBM * D * 4;
+  static constexpr int kOffDQ = kOffStat + kQStages * 2 * kBM * 4;  // [D][64] fp32 dQ^T staging
+  static constexpr int kDQTile = kBM * D * 4;
+  static constexpr int kOffBar = kOffDQ + 1 * kDQTile;
   static constexpr int kUsed = kOffBar + 256 + 1024;
   // One CTA per SM: the kernel owns all 512 TMEM columns.
   static constexpr int kSmem = kUsed > 120 * 1024 ? kUsed : 120 * 1024;
@@ -78,7 +87,8 @@ struct TcBwdArgs {
   ts_view4 dk, dv;
   float* stats;      // [B*Hq][2][t_pad]: -LSE*log2e (-inf: no row / fully masked), -delta (0: no row)
   int t_pad;         // Tq rounded up to the 64-row query tile
-  float* dq_acc;     // [B, Hq, Tq, D]
+  float* dq_acc;     // [B*Hq][t_pad / 64][D][64] fp32: per 64-row tile, channel d's 64 rows as
+                     // 16-byte chunks, chunk j stored at index (j ^ (d & 7))
   int n_k_tiles;
   uint32_t* fault;
   DropoutArgs drop;  // used by the kDrop instantiation only
@@ -87,7 +97,7 @@ struct TcBwdArgs {
 }  // namespace
 
 template <int D, bool kBF16, bool kDrop>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(512, 1)
     tc_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                   TcBwdArgs args) {
@@ -130,8 +140,8 @@ __global__ void __launch_bounds__(384, 1)
       ptx::mbar_init(&bars->qdo_empty[s], 1);
     }
     ptx::mbar_init(&bars->s_full, 1);
-    ptx::mbar_init(&bars->s_free, 4);
-    ptx::mbar_init(&bars->p_full, 4);
+    ptx::mbar_init(&bars->s_free, 8);
+    ptx::mbar_init(&bars->p_full, 8);
     ptx::mbar_init(&bars->b_done, 1);
     ptx::mbar_init(&bars->dq_free, 4);
     ptx::mbar_init(&bars->drain, 1);
@@ -241,9 +251,12 @@ __global__ void __launch_bounds__(384, 1)
       ptx::mma_commit(&bars->drain);
       (void)wait_bar(&bars->drain, 0, nullptr, FAULT_FWD_DRAIN);
     }
-  } else if (warp >= 4 && warp < 8) {
+  } else if ((warp >= 4 && warp < 8) || warp >= 12) {
     // ------------------- P^T / dS^T (thread = key row) ---------------------
-    const int row = (warp - 4) * 32 + lane;
+    // Two warpgroups over the same 128 key rows: warps 4-7 take query columns
+    // [0, 32) of every tile, warps 12-15 columns [32, 64).
+    const int half = warp >= 12 ? 1 : 0;
+    const int row = (warp & 3) * 32 + lane;
     const int key = k0 + row;
     const uint32_t t_row = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const float sl2 = (float)p.scale * kLog2e, scale = (float)p.scale;
@@ -265,29 +278,19 @@ __global__ void __launch_bounds__(384, 1)
         // i + offset >= key), none when the key is past the row's end.
         const int64_t cm = p.is_causal ? (int64_t)key - offset - q0 : 0;
         const int c_min = key_ok ? (int)i64max(0, i64min(kBM, cm)) : kBM;
-        // Not unrolled over the two halves: one copy of the element loop keeps
-        // the softmax warps' code small next to the other roles' code.
-#pragma unroll 1
-        for (int half = 0; half < 2; ++half) {
+        {
           uint32_t rs[32], rd[32];
           ptx::tmem_ld32(t_row + C::kColS + 32 * half, rs);
           ptx::tmem_ld32(t_row + C::kColDP + 32 * half, rd);
           ptx::tmem_wait_ld();
-          if (half == 1) {
-            ptx::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(&bars->s_free);
-          }
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&bars->s_free);
           uint32_t pk[16], dk[16];
-          // This half's -LSE*log2e and -delta as packed pairs (float4 broadcasts from shared memory).
-          uint64_t nl2[16], nd2[16];
-#pragma unroll
-          for (int c = 0; c < 32; c += 4) {
-            const float4 a = *reinterpret_cast<const float4*>(nlse2 + 32 * half + c);
-            const float4 d4 = *reinterpret_cast<const float4*>(ndlt + 32 * half + c);
-            nl2[c / 2] = ptx::f2pack(a.x, a.y), nl2[c / 2 + 1] = ptx::f2pack(a.z, a.w);
-            nd2[c / 2] = ptx::f2pack(d4.x, d4.y), nd2[c / 2 + 1] = ptx::f2pack(d4.z, d4.w);
-          }
+          // -LSE*log2e and -delta of this group's columns, read as packed pairs
+          // (64-bit shared-memory broadcasts) inside the element loop.
+          const uint64_t* nl2 = reinterpret_cast<const uint64_t*>(nlse2 + 32 * half);
+          const uint64_t* nd2 = reinterpret_cast<const uint64_t*>(ndlt + 32 * half);
           // Dropout (kDrop): keep bit of (this key, column 32*half + c) in bit c.  The
           // generator gives the bits of 8 consecutive keys per call, so the 8 lanes
           // of a key octet each draw one column of every 8 and swap bytes.
@@ -341,7 +344,7 @@ __global__ void __launch_bounds__(384, 1)
             dk[c / 2] = kBF16 ? ptx::pack_bf16(d0, d1) : ptx::pack_f16(d0, d1);
           }
           // P^T / dS^T buffers are free once the previous iteration's dV/dK/dQ MMAs completed.
-          if (half == 0 && it >= 1)
+          if (it >= 1)
             ok = __all_sync(0xffffffffu, wait_bar(&bars->b_done, (it - 1) & 1, args.fault, FAULT_FWD_O));
           if (ok) {
             // P^T and dS^T into TMEM (A operands of dV += P^T dO, dK += dS^T Q);
@@ -373,8 +376,8 @@ __global__ void __launch_bounds__(384, 1)
     // tcgen05.ld is warp-collective (.sync.aligned): every lane loads, and only
     // the global stores are predicated on the key being inside the tensor.
     const bool store_row = key < p.kv_len;
-#pragma unroll
-    for (int which = 0; which < 2; ++which) {
+    {
+      const int which = half;
       const ts_view4& dst = which == 0 ? args.dk : args.dv;
       T* out = reinterpret_cast<T*>(dst.data) + (int64_t)b * dst.stride[0] + (int64_t)hk * dst.stride[1] +
                (int64_t)key * dst.stride[2];
@@ -404,11 +407,11 @@ __global__ void __launch_bounds__(384, 1)
         }
       }
     }
-  } else if (warp >= 8) {
+  } else if (warp >= 8 && warp < 12) {
     // ----------------------- dQ epilogue (thread = channel) ----------------
-    // dQ^T (lane = channel) -> a row-major [64][D] fp32 staging tile -> one
-    // bulk reduce-add into the fp32 dQ accumulator per
-    // iteration, issued by the group's first thread.  Every dQ warp runs all
+    // dQ^T (lane = channel) -> a channel-major [D][64] fp32 staging tile (the
+    // accumulator's tile layout) -> one bulk reduce-add into the fp32 dQ
+    // accumulator per iteration, issued by the group's first thread.  Every dQ warp runs all
     // n_it iterations and reaches both named barriers; after a failed wait it
     // only skips the work.
     const int d = (warp - 8) * 32 + lane;
@@ -433,18 +436,24 @@ __global__ void __launch_bounds__(384, 1)
       asm volatile("bar.sync 2, 128;" ::: "memory");
       float* st = stage;
       if (ok && d < D) {
+        // Channel d's 64 rows as 16 chunks of 4; chunk j at (j ^ (d & 7)) so
+        // the 8 threads of each 128-bit store phase hit distinct banks.
+        float4* rowp = reinterpret_cast<float4*>(st + d * kBM);
 #pragma unroll
-        for (int c = 0; c < 32; ++c) st[c * D + d] = __uint_as_float(r0[c]);
+        for (int j = 0; j < 8; ++j)
+          rowp[j ^ (d & 7)] = make_float4(__uint_as_float(r0[4 * j]), __uint_as_float(r0[4 * j + 1]),
+                                          __uint_as_float(r0[4 * j + 2]), __uint_as_float(r0[4 * j + 3]));
 #pragma unroll
-        for (int c = 0; c < 32; ++c) st[(32 + c) * D + d] = __uint_as_float(r1[c]);
+        for (int j = 0; j < 8; ++j)
+          rowp[(8 + j) ^ (d & 7)] = make_float4(__uint_as_float(r1[4 * j]), __uint_as_float(r1[4 * j + 1]),
+                                                __uint_as_float(r1[4 * j + 2]), __uint_as_float(r1[4 * j + 3]));
       }
       ptx::fence_proxy_async_smem();
       asm volatile("bar.sync 2, 128;" ::: "memory");
       if (leader && ok) {
-        const int h = it_head(it), q0 = it_q0(it);
-        const int rows = min(kBM, p.q_len - q0);
-        ptx::bulk_reduce_add_f32(args.dq_acc + (((int64_t)b * p.q_heads + h) * p.q_len + q0) * D, st,
-                                 (uint32_t)(rows * D * 4));
+        const int h = it_head(it), qt = it_q0(it) / kBM;
+        ptx::bulk_reduce_add_f32(args.dq_acc + (((int64_t)b * p.q_heads + h) * (args.t_pad / kBM) + qt) * (D * kBM),
+                                 st, (uint32_t)(D * kBM * 4));
         ptx::bulk_commit();
       }
     }
@@ -459,18 +468,29 @@ __global__ void __launch_bounds__(384, 1)
   }
 }
 
-// dq[b,h,i,:] = dq_acc (fp32) converted to the input dtype.
-template <typename T>
-__global__ void dq_convert_kernel(const float* __restrict__ acc, ts_view4 dq, int heads, int len, int dim,
-                                  int64_t total) {
-  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int d = (int)(idx % dim);
-    const int64_t r = idx / dim;
-    const int i = (int)(r % len), h = (int)((r / len) % heads), b = (int)(r / ((int64_t)len * heads));
-    reinterpret_cast<T*>(dq.data)[(int64_t)b * dq.stride[0] + (int64_t)h * dq.stride[1] +
-                                  (int64_t)i * dq.stride[2] + (int64_t)d * dq.stride[3]] =
-        Elem<T>::from_acc(acc[idx]);
+// dq[b,h,i,:] = dq_acc (fp32, one channel-major [D][64] tile per 64 rows) converted
+// to the input dtype: one CTA per (tile, b*h) transposes its tile through
+// shared memory so both the read and the write are coalesced.
+template <typename T, int D>
+__global__ void __launch_bounds__(256) dq_convert_kernel(const float* __restrict__ acc, ts_view4 dq, int heads,
+                                                         int len, int n_tiles) {
+  __shared__ float tile[kBM][D + 1];
+  const int bh = blockIdx.x, t = blockIdx.y;
+  const float4* src = reinterpret_cast<const float4*>(acc + ((int64_t)bh * n_tiles + t) * (D * kBM));
+  for (int idx = threadIdx.x; idx < D * (kBM / 4); idx += blockDim.x) {
+    const int d = idx / (kBM / 4), j = (idx % (kBM / 4)) ^ (d & 7);
+    const float4 v = src[idx];
+    tile[4 * j][d] = v.x;
+    tile[4 * j + 1][d] = v.y;
+    tile[4 * j + 2][d] = v.z;
+    tile[4 * j + 3][d] = v.w;
+  }
+  __syncthreads();
+  const int b = bh / heads, h = bh % heads;
+  T* out = reinterpret_cast<T*>(dq.data) + (int64_t)b * dq.stride[0] + (int64_t)h * dq.stride[1];
+  for (int idx = threadIdx.x; idx < kBM * D; idx += blockDim.x) {
+    const int r = idx / D, d = idx % D, i = t * kBM + r;
+    if (i < len) out[(int64_t)i * dq.stride[2] + (int64_t)d * dq.stride[3]] = Elem<T>::from_acc(tile[r][d]);
   }
 }
 
@@ -498,7 +518,7 @@ static int t_padded(int q_len) { return ceil_div(q_len, kBM) * kBM; }
 
 size_t tc_bwd_workspace(const ts_attn_bwd_params& bp) {
   const ts_attn_params& p = bp.fwd;
-  const size_t rows = (size_t)p.batch * p.q_heads * p.q_len;
+  const size_t rows = (size_t)p.batch * p.q_heads * t_padded(p.q_len);
   const size_t stats = (size_t)p.batch * p.q_heads * 2 * t_padded(p.q_len);
   return align256(stats * sizeof(float)) + align256(rows * p.head_dim * sizeof(float));
 }
@@ -545,7 +565,7 @@ static cudaError_t launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, cons
   cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(kern), BwdCfg<D>::kSmem);
   if (e != cudaSuccess) return e;
   dim3 grid(a.n_k_tiles, a.p.kv_heads, a.p.batch);
-  kern<<<grid, 384, BwdCfg<D>::kSmem, st>>>(mq, mk, mv, mdo, a);
+  kern<<<grid, 512, BwdCfg<D>::kSmem, st>>>(mq, mk, mv, mdo, a);
   return cudaGetLastError();
 }
 
@@ -553,8 +573,8 @@ cudaError_t tc_backward(const ts_attn_bwd_params& bp, void* ws, size_t ws_bytes,
                         cudaStream_t st, const DropoutArgs* drop) {
   const ts_attn_params& p = bp.fwd;
   if (ws_bytes < tc_bwd_workspace(bp)) return cudaErrorInvalidValue;
-  const size_t rows = (size_t)p.batch * p.q_heads * p.q_len;
   const int t_pad = t_padded(p.q_len);
+  const size_t rows = (size_t)p.batch * p.q_heads * t_pad;
   const size_t n_stats = (size_t)p.batch * p.q_heads * 2 * t_pad;
   float* stats = reinterpret_cast<float*>(ws);
   float* dq_acc = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(ws) + align256(n_stats * sizeof(float)));
@@ -592,12 +612,19 @@ cudaError_t tc_backward(const ts_attn_bwd_params& bp, void* ws, size_t ws_bytes,
   else
     e = bf ? launch_bwd<128, true>(mq, mk, mv, mdo, a, st) : launch_bwd<128, false>(mq, mk, mv, mdo, a, st);
   if (e != cudaSuccess) return e;
-  const int64_t total = (int64_t)rows * p.head_dim;
-  const int blocks = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
-  if (bf)
-    dq_convert_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(dq_acc, bp.dq, p.q_heads, p.q_len, p.head_dim, total);
-  else
-    dq_convert_kernel<__half><<<blocks, 256, 0, st>>>(dq_acc, bp.dq, p.q_heads, p.q_len, p.head_dim, total);
+  const dim3 cgrid((unsigned)(p.batch * p.q_heads), (unsigned)(t_pad / kBM));
+  const int n_tiles = t_pad / kBM;
+  if (p.head_dim == 64) {
+    if (bf)
+      dq_convert_kernel<__nv_bfloat16, 64><<<cgrid, 256, 0, st>>>(dq_acc, bp.dq, p.q_heads, p.q_len, n_tiles);
+    else
+      dq_convert_kernel<__half, 64><<<cgrid, 256, 0, st>>>(dq_acc, bp.dq, p.q_heads, p.q_len, n_tiles);
+  } else {
+    if (bf)
+      dq_convert_kernel<__nv_bfloat16, 128><<<cgrid, 256, 0, st>>>(dq_acc, bp.dq, p.q_heads, p.q_len, n_tiles);
+    else
+      dq_convert_kernel<__half, 128><<<cgrid, 256, 0, st>>>(dq_acc, bp.dq, p.q_heads, p.q_len, n_tiles);
+  }
   return cudaGetLastError();
 }
 
