@@ -1019,11 +1019,12 @@ static int sm_count() {
 // The persistent schedule pays off where each CTA of the one-tile-per-CTA grid
 // would carry few key tiles, so its set-up and epilogue show (measured at
 // B=8, H=16, T=4096: 839 against 786 TFLOP/s), and loses where rows are long
-// (T=32768: 862 against 952): causal, at most 32 query tiles, no per-row
-// lengths (units of unequal length would unbalance the static schedule), and
-// at least two units per SM.
+// (T=32768: 862 against 952; a 4096-row chunk at causal offsets up to 28672
+// keys, 4 GPUs: 96 against 70 ms per prefill): causal, rows of at most 4096
+// keys (offset + query length), no per-row lengths (units of unequal length
+// would unbalance the static schedule), and at least two units per SM.
 static bool use_persistent(const TcFwdArgs& a, int sms) {
-  return a.p.is_causal && !a.p.kv_lens && a.n_q_tiles <= 32 && a.n_units >= 2 * sms;
+  return a.p.is_causal && !a.p.kv_lens && a.p.causal_offset + a.p.q_len <= 32 * kBN && a.n_units >= 2 * sms;
 }
 
 template <int D, bool BF16>

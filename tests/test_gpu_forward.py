@@ -83,16 +83,16 @@ def test_forward_tcgen05(shape, name):
     assert engine.fwd_path(q, k, v, is_causal=causal, causal_offset=off) == "tcgen05"
 
 
-# Causal shapes with at least two work units per SM (a unit = query tiles
-# X-1-t and t of one (batch, head); X query tiles of 128 rows): the forward
-# runs them on the persistent tcgen05 kernel.
+# Causal shapes with rows of at most 4096 keys and at least two work units per
+# SM (a unit = query tiles X-1-t and t of one (batch, head); X query tiles of
+# 128 rows): the forward runs them on the persistent tcgen05 kernel.
 PERSISTENT_SHAPES = [
     (4, 20, 20, 1024, 1024, 128, 128, True, 0),   # 8 query tiles, 320 units
     (8, 24, 8, 640, 640, 64, 64, True, 0),        # 5 tiles: the middle one is a unit alone; GQA
     (3, 64, 32, 300, 429, 128, 128, True, 129),   # offset, ragged last tile, GQA
     (160, 2, 1, 129, 129, 64, 64, True, 0),       # second tile holds one row
     (1, 300, 300, 100, 100, 64, 64, True, 0),     # one tile per (batch, head)
-    (1, 20, 20, 4096, 4096, 64, 64, True, 0),     # 32 query tiles, the most the schedule takes
+    (1, 20, 20, 4096, 4096, 64, 64, True, 0),     # rows of 4096 keys, the longest the schedule takes
 ]
 
 
@@ -109,7 +109,7 @@ def test_forward_tcgen05_persistent(shape, name):
     so that the largest shape stays within a few hundred MB on the host."""
     b, hq, hkv, tq, tk, d, dv, causal, off = shape
     units, x = _persistent_units(shape)
-    assert x <= 32 and units >= 2 * torch.cuda.get_device_properties(0).multi_processor_count
+    assert off + tq <= 4096 and units >= 2 * torch.cuda.get_device_properties(0).multi_processor_count
     q, k, v = _inputs(shape, name, 5)
     tq_, tk_, tv_ = (to_cuda(a, name) for a in (q, k, v))
     assert engine.fwd_path(tq_, tk_, tv_, is_causal=True, causal_offset=off) == "tcgen05"
