@@ -34,6 +34,8 @@
 // are K-major (8-row x 128-byte atoms, 1024 B apart); V is read MN-major
 // (64-channel blocks 16 KB apart, 8-key groups 1024 B apart).  No TMA load
 // uses cluster multicast.
+#include <cstdlib>
+#include <cstring>
 #include <type_traits>
 
 #include "ptx.cuh"
@@ -1027,11 +1029,25 @@ static bool use_persistent(const TcFwdArgs& a, int sms) {
   return a.p.is_causal && !a.p.kv_lens && a.p.causal_offset + a.p.q_len <= 32 * kBN && a.n_units >= 2 * sms;
 }
 
+// Kernel choice for problems of two or more query tiles: the two-tile kernel
+// (attn_fwd_pair.cu) by default; TS_FWD_KERNEL = "tile" or "persistent" in the
+// environment selects one of this file's kernels instead (read at every call,
+// for tests and measurements of all three).
+enum class FwdKernel { kDefault, kPair, kTile, kPersistent };
+static FwdKernel fwd_kernel_env() {
+  const char* e = getenv("TS_FWD_KERNEL");
+  if (!e) return FwdKernel::kDefault;
+  if (!strcmp(e, "pair")) return FwdKernel::kPair;
+  if (!strcmp(e, "tile")) return FwdKernel::kTile;
+  if (!strcmp(e, "persistent")) return FwdKernel::kPersistent;
+  return FwdKernel::kDefault;
+}
+
 template <int D, bool BF16>
 static cudaError_t launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                             const TcFwdArgs& a, cudaStream_t st) {
+                             const TcFwdArgs& a, cudaStream_t st, bool persistent) {
   const int sms = sm_count();
-  if (use_persistent(a, sms)) {
+  if (persistent) {
     auto pk = a.drop.p > 0.f ? tc_fwd_persistent_kernel<D, BF16, true> : tc_fwd_persistent_kernel<D, BF16, false>;
     cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(pk), Cfg<D>::kSmem);
     if (e != cudaSuccess) return e;
@@ -1059,9 +1075,19 @@ cudaError_t tc_forward(const ts_attn_params& p, uint32_t* fault, cudaStream_t st
   a.n_units = p.batch * p.q_heads * a.half_x;
   a.fault = fault;
   a.drop = drop ? *drop : DropoutArgs{};
+  // Two or more query tiles run on the two-tile kernel, which measured faster
+  // than both kernels of this file: C5 shape (T=32768) 1189 against 1066
+  // TFLOP/s, C3 (T=4096) 886 against 843 (persistent) and 790 (one tile).
+  // A single query tile (short prefill chunks, the grouped-query decode view)
+  // keeps the one-tile kernel.
+  const FwdKernel env = fwd_kernel_env();
+  if (a.n_q_tiles >= 2 && (env == FwdKernel::kDefault || env == FwdKernel::kPair))
+    return tc_forward_pair(p, mq, mk, mv, fault, st, drop);
+  const bool persistent = env == FwdKernel::kPersistent || (env == FwdKernel::kDefault && use_persistent(a, sm_count()));
   const bool bf = p.dtype == TS_BF16;
-  if (p.head_dim == 64) return bf ? launch_tc<64, true>(mq, mk, mv, a, st) : launch_tc<64, false>(mq, mk, mv, a, st);
-  return bf ? launch_tc<128, true>(mq, mk, mv, a, st) : launch_tc<128, false>(mq, mk, mv, a, st);
+  if (p.head_dim == 64)
+    return bf ? launch_tc<64, true>(mq, mk, mv, a, st, persistent) : launch_tc<64, false>(mq, mk, mv, a, st, persistent);
+  return bf ? launch_tc<128, true>(mq, mk, mv, a, st, persistent) : launch_tc<128, false>(mq, mk, mv, a, st, persistent);
 }
 
 }  // namespace tsa

@@ -207,6 +207,19 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int m, int n, bool a
          ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
+// Per-warpgroup register budget (all four warps of the warpgroup execute the
+// same instruction).  The budgets of a kernel's warps after these, summed,
+// must stay within the registers it was launched with (threads x registers
+// per thread), or the growing warpgroup waits for registers forever.
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ----------------------------- math helpers --------------------------------
 __device__ __forceinline__ float ex2(float x) {
   float y;

@@ -1,5 +1,7 @@
 // Entry points of the tcgen05 prefill forward (attn_fwd_tc.cu).
 #pragma once
+#include <cuda.h>
+
 #include "common.cuh"
 #include "dropout.cuh"
 
@@ -9,6 +11,11 @@ bool tc_fwd_supported(const ts_attn_params& p);
 // `drop` set: attention dropout on P before P.V (the generic kernels' mask).
 cudaError_t tc_forward(const ts_attn_params& p, uint32_t* fault, cudaStream_t stream,
                        const DropoutArgs* drop = nullptr);
+
+// The two-query-tile kernel (attn_fwd_pair.cu) on the maps tc_forward built
+// (128-row boxes of Q, K and V).
+cudaError_t tc_forward_pair(const ts_attn_params& p, const CUtensorMap& mq, const CUtensorMap& mk,
+                            const CUtensorMap& mv, uint32_t* fault, cudaStream_t stream, const DropoutArgs* drop);
 
 // Fewest (batch, KV head) pairs for which a grouped-query decode step runs on
 // the prefill kernel (one CTA per pair, no split along the keys): with fewer,

@@ -128,16 +128,21 @@ TC_CASES = [
     ("bfloat16", 1, 4, 2, 200, 331, 64, True, 131, 0.2),
     ("bfloat16", 2, 2, 2, 130, 130, 128, False, 0, 0.5),
     ("float16", 1, 2, 1, 257, 257, 128, True, 0, 0.1),
-    # 148 pairs x 2 units: the persistent forward's kDrop instantiation
+    # 148 pairs x 2 units: with TS_FWD_KERNEL=persistent, the persistent forward's kDrop instantiation
     ("bfloat16", 1, 148, 74, 300, 300, 64, True, 0, 0.2),
 ]
 
 
+@pytest.mark.parametrize("kernel", ["default", "other"])
 @pytest.mark.parametrize("case", TC_CASES, ids=lambda c: f"{c[0]}-D{c[6]}-T{c[4]}x{c[5]}-p{c[9]}")
-def test_tcgen05_dropout_matches_oracle(case):
+def test_tcgen05_dropout_matches_oracle(case, kernel, monkeypatch):
     """The tensor-core forward and backward (kDrop instantiations) draw the same
-    mask as the materialised one and match the oracle's dense dropout VJP."""
+    mask as the materialised one and match the oracle's dense dropout VJP.
+    "default" runs the two-tile forward on these multi-tile shapes; "other"
+    selects the one-tile kernel (or the persistent one for the 148-pair case)."""
     name, b, hq, hkv, tq, tk, d, causal, offset, p = case
+    if kernel == "other":
+        monkeypatch.setenv("TS_FWD_KERNEL", "persistent" if hq == 148 else "tile")
     rng = np.random.default_rng(tq + tk + d)
     q, k, v = (rng.normal(size=s) for s in ((b, hq, tq, d), (b, hkv, tk, d), (b, hkv, tk, d)))
     g = rng.normal(size=(b, hq, tq, d))

@@ -75,9 +75,16 @@ def test_forward_generic(shape, name):
     _run(shape, name)
 
 
+# Problems of two or more 128-row query tiles run on the two-tile kernel
+# (attn_fwd_pair.cu) by default; TS_FWD_KERNEL=tile selects the one-tile
+# kernel so that it keeps its coverage (it still runs every single-tile
+# problem and the grouped-query decode view).
+@pytest.mark.parametrize("kernel", ["default", "tile"])
 @pytest.mark.parametrize("name", ["bfloat16", "float16"])
 @pytest.mark.parametrize("shape", TC_SHAPES, ids=str)
-def test_forward_tcgen05(shape, name):
+def test_forward_tcgen05(shape, name, kernel, monkeypatch):
+    if kernel != "default":
+        monkeypatch.setenv("TS_FWD_KERNEL", kernel)
     q, k, v = _run(shape, name, seed=1)
     b, hq, hkv, tq, tk, d, dv, causal, off = shape
     assert engine.fwd_path(q, k, v, is_causal=causal, causal_offset=off) == "tcgen05"
@@ -85,7 +92,8 @@ def test_forward_tcgen05(shape, name):
 
 # Causal shapes with rows of at most 4096 keys and at least two work units per
 # SM (a unit = query tiles X-1-t and t of one (batch, head); X query tiles of
-# 128 rows): the forward runs them on the persistent tcgen05 kernel.
+# 128 rows): TS_FWD_KERNEL=persistent runs them on the persistent tcgen05
+# kernel; by default they run on the two-tile kernel.
 PERSISTENT_SHAPES = [
     (4, 20, 20, 1024, 1024, 128, 128, True, 0),   # 8 query tiles, 320 units
     (8, 24, 8, 640, 640, 64, 64, True, 0),        # 5 tiles: the middle one is a unit alone; GQA
@@ -102,11 +110,15 @@ def _persistent_units(shape):
     return b * hq * ((x + 1) // 2), x
 
 
+@pytest.mark.parametrize("kernel", ["default", "persistent"])
 @pytest.mark.parametrize("name", ["bfloat16", "float16"])
 @pytest.mark.parametrize("shape", PERSISTENT_SHAPES, ids=str)
-def test_forward_tcgen05_persistent(shape, name):
-    """Parity of the persistent schedule; the oracle runs one head at a time
-    so that the largest shape stays within a few hundred MB on the host."""
+def test_forward_tcgen05_persistent(shape, name, kernel, monkeypatch):
+    """Parity of the persistent schedule and of the two-tile kernel on the same
+    shapes; the oracle runs one head at a time so that the largest shape stays
+    within a few hundred MB on the host."""
+    if kernel != "default":
+        monkeypatch.setenv("TS_FWD_KERNEL", kernel)
     b, hq, hkv, tq, tk, d, dv, causal, off = shape
     units, x = _persistent_units(shape)
     assert off + tq <= 4096 and units >= 2 * torch.cuda.get_device_properties(0).multi_processor_count
