@@ -70,9 +70,9 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the scored kernel, from the ncu
 # captures summarised under profiles/, per unit of work so a launch of any size scales by its units.
 PROFILED_TRAFFIC = {
-    # tc_fwd_kernel<128,bf16> at T=32768, 8 (b,h) pairs: (201.4 + 51.3) MB / 8 pairs
-    "c5": dict(bytes_per_unit=31.59e6, unit="(b,h) pair at T=32768",
-               source="profiles/tc_fwd_bwd_kernels_c5slice.md"),
+    # tc_fwd_pair_kernel<128,bf16> at T=32768, 8 (b,h) pairs: (202.6 + 49.2) MB / 8 pairs
+    "c5": dict(bytes_per_unit=31.48e6, unit="(b,h) pair at T=32768",
+               source="profiles/tc_fwd_pair_kernel_c5slice.md"),
     # tc_bwd_kernel<128,bf16> at the C3 shape: 809.6 MB read + 494.3 MB written per launch
     "c3": dict(bytes_per_unit=1303.9e6, unit="C3 backward launch", source="profiles/tc_bwd_kernel_c3.md"),
     # split-K decode: DRAM bytes / algorithmic K+V bytes = (268.6 + 4.1) / 268.5
@@ -541,7 +541,7 @@ def run_engine(args, rank: int, world: int, local_rank: int):
                        "hbm_gbs_per_gpu": kv_bytes / world / (dec / 1e3) / 1e9,
                        "frac_of_measured_hbm": kv_bytes / world / (dec / 1e3) / 1e9 / peaks["hbm_gbs"],
                        "ms_per_token_step": dec / S},
-            "roofline": {"bound": "tensor", "kernel": "tc_fwd_kernel<128,bf16>", "achieved": achieved,
+            "roofline": {"bound": "tensor", "kernel": "tc_fwd_pair_kernel<128,bf16>", "achieved": achieved,
                          "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                          "peak_source": f"{peak_src} bf16_tflops_sustained",
                          "traffic": profiled_traffic("c5", n) if T == 32768 else None,
@@ -779,7 +779,7 @@ def run_c3(args):
                      "peak_source": f"{src} bf16_tflops (burst; the call runs ~ms)",
                      "traffic": profiled_traffic("c3", 1) if args.workload == "c3" else None,
                      "algorithmic": f"10*D*causal_pairs = {10 * pairs_flops:.4g} FLOP per backward call"},
-        "gpu_launches": 4 * args.steps,  # tc_fwd_kernel, bwd_stats_kernel, tc_bwd_kernel, dq_convert_kernel
+        "gpu_launches": 4 * args.steps,  # tc_fwd_pair_kernel, bwd_stats_kernel, tc_bwd_kernel, dq_convert_kernel
         "clocks": clocks,
     }
     if not args.no_cpu_baseline and args.workload == "c3":
