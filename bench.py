@@ -361,7 +361,7 @@ def run_engine(args, rank: int, world: int, local_rank: int):
     import torch.distributed as dist
 
     from tensorsmith_b200 import engine
-    from tensorsmith_b200.distributed import ShardPlan, gather_to_root
+    from tensorsmith_b200.distributed import RootWindow, ShardPlan, gather_to_root
 
     cfg = WORKLOADS[args.workload]
     B, H, D, T, S = cfg["batch"], cfg["heads"], cfg["head_dim"], cfg["prefill"], cfg["decode_steps"]
@@ -407,8 +407,29 @@ def run_engine(args, rank: int, world: int, local_rank: int):
     rows_per_chunk = T if world == 1 else min(T, PREFILL_CHUNK_ROWS)
     chunks = [(r0, min(T, r0 + rows_per_chunk)) for r0 in range(0, T, rows_per_chunk)][::-1]
     o_parts = ([torch.empty(1, n, r1 - r0, D, dtype=bf, device=dev) for r0, r1 in chunks] if world > 1 else None)
-    o_full_parts = ([torch.empty(world, n, r1 - r0, D, dtype=bf, device=dev) for r0, r1 in chunks]
-                    if rank == 0 and world > 1 else None)
+    # Prefill outputs reach rank 0 by copy-engine writes into one buffer of rank
+    # 0 (CUDA IPC over NVLink; no SMs taken from the forward that runs
+    # meanwhile); chunk c of rank r lands at [c][r] of it.  Where a rank cannot
+    # map rank 0's buffer, every rank keeps the NCCL gathers.
+    window = None
+    chunk_elems = [world * n * (r1 - r0) * D for r0, r1 in chunks]
+    chunk_base = [sum(chunk_elems[:c]) for c in range(len(chunks))]
+    if world > 1:
+        window = RootWindow((sum(chunk_elems),), bf, dev)
+        if not window.ok:
+            window.close()
+            window = None
+    if window is not None:
+        o_full_parts = ([window.buffer[chunk_base[c]: chunk_base[c] + chunk_elems[c]].view(world, n, r1 - r0, D)
+                         for c, (r0, r1) in enumerate(chunks)] if rank == 0 else None)
+    else:
+        o_full_parts = ([torch.empty(world, n, r1 - r0, D, dtype=bf, device=dev) for r0, r1 in chunks]
+                        if rank == 0 and world > 1 else None)
+    copy_stream = torch.cuda.Stream(device=dev) if window is not None else None
+    chunk_done = [torch.cuda.Event() for _ in chunks]
+    # Chunks alternate between two streams: they are independent, so each
+    # chunk's CTAs fill the SMs that the previous chunk's last wave leaves idle.
+    chunk_streams = [torch.cuda.Stream(device=dev) for _ in range(2)] if world > 1 else None
     launches_per_step = len(chunks) + S * (2 + (1 if splits else 0))
 
     def prefill_rows(pr):
@@ -438,12 +459,26 @@ def run_engine(args, rank: int, world: int, local_rank: int):
         if world == 1:
             engine.forward(q, kc[:, :, :T], vc[:, :, :T], is_causal=True, need_lse=False, out=o)
         else:
+            main = torch.cuda.current_stream()
+            for cs in chunk_streams:
+                cs.wait_stream(main)
             for c, (r0, r1) in enumerate(chunks):
-                engine.forward(q[:, :, r0:r1], kc[:, :, :r1], vc[:, :, :r1], is_causal=True, causal_offset=r0,
-                               need_lse=False, out=o_parts[c])
-                works.append(gather_async(o_parts[c], None if o_full_parts is None else o_full_parts[c],
-                                          prefill_group))
+                with torch.cuda.stream(chunk_streams[c % 2]):
+                    engine.forward(q[:, :, r0:r1], kc[:, :, :r1], vc[:, :, :r1], is_causal=True, causal_offset=r0,
+                                   need_lse=False, out=o_parts[c])
+                    if window is not None:
+                        chunk_done[c].record()
+                        copy_stream.wait_event(chunk_done[c])
+                        window.put(o_parts[c], 2 * (chunk_base[c] + rank * n * (r1 - r0) * D), copy_stream)
+                    else:
+                        works.append(gather_async(o_parts[c], None if o_full_parts is None else o_full_parts[c],
+                                                  prefill_group))
+            for cs in chunk_streams:
+                main.wait_stream(cs)
         ev[1].record()
+        if window is not None:
+            torch.cuda.current_stream().wait_stream(copy_stream)
+            window.done(dev)
         for work in works:
             work.wait()
         ev[2].record()
@@ -483,6 +518,19 @@ def run_engine(args, rank: int, world: int, local_rank: int):
     barrier()
     clocks = sampler.stop() if sampler else None
     engine.check_device_status(dev)
+    prefill_transport = "copy engine (CUDA IPC)" if window is not None else "NCCL"
+    if window is not None:
+        # Every rank's last chunk as rank 0 received it must equal the rank's own output.
+        sums = [None] * world
+        dist.all_gather_object(sums, [float(o_parts[c].double().sum()) for c in range(len(chunks))])
+        if rank == 0:
+            for c in range(len(chunks)):
+                assert torch.equal(o_full_parts[c][0], o_parts[c][0]), "copy-engine gather: rank 0's shard differs"
+                for r in range(1, world):
+                    got = float(o_full_parts[c][r].double().sum())
+                    assert abs(got - sums[r][c]) <= 1e-9 * max(1.0, abs(sums[r][c])), \
+                        f"copy-engine gather: chunk {c} of rank {r} differs ({got} vs {sums[r][c]})"
+        window.close()
 
     kern_ms = [e[0].elapsed_time(e[1]) for e in evs]
     prefill_ms = [e[0].elapsed_time(e[2]) for e in evs]
@@ -527,10 +575,10 @@ def run_engine(args, rank: int, world: int, local_rank: int):
             "config": {
                 "workload": (f"{args.workload}: causal prefill bf16 B={B} H={H} D={D} T={T}, then {S} decode "
                              f"steps (KV append + split-K decode), (b,h) pairs sharded over {world} GPU(s), "
-                             "outputs gathered to rank 0 over NCCL (with N > 1 the prefill runs in "
-                             f"{len(chunks)} query-row chunks, longest first, each chunk's gather overlapping the "
-                             f"next chunk on a process group held to {PREFILL_GATHER_CTAS} NCCL CTAs; decode "
-                             "gathers queued and waited for at the end of the step)"),
+                             "outputs gathered to rank 0 (with N > 1 the prefill runs in "
+                             f"{len(chunks)} query-row chunks, longest first, alternating over two streams, each chunk's output sent to rank 0 "
+                             f"while the next chunk computes, by {prefill_transport}; decode gathers over NCCL, "
+                             "queued and waited for at the end of the step)"),
                 "global_batch": B, "seq_len": T, "parallelism": f"bxh-shard{world}",
                 "l2": "inputs larger than L2 (Q/K/V/cache >= 8 GB per step)",
             },

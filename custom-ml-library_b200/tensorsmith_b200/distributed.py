@@ -3,8 +3,10 @@
 Every (batch row, KV head) pair -- with the query heads of its group -- is an
 independent attention problem for prefill, backward and decode, so ranks own
 contiguous blocks of pairs and never reduce.  The only collective is the
-gather of each rank's outputs to the caller's rank (NCCL over NVLink through
-``torch.distributed``).  tensorsmith itself has no such path: its only
+gather of each rank's outputs to the caller's rank: NCCL over NVLink through
+``torch.distributed`` (``gather_to_root``), or copy-engine writes into a
+buffer of the root rank (``RootWindow``), which take no SMs from the kernels
+that run meanwhile.  tensorsmith itself has no such path: its only
 multi-process code is a host-staged TCP all-reduce for data parallelism
 (src/tensorsmith/distributed.py:22-218).
 """
@@ -136,3 +138,108 @@ def gather_to_root(local: torch.Tensor, plan: ShardPlan, out=None, root: int = 0
         for c, t in zip(chunks, targets):
             c.copy_(t)
     return out
+
+
+class RootWindow:
+    """A contiguous buffer on the root rank that every rank writes into with
+    copy-engine transfers over NVLink (CUDA IPC), so a gather overlaps the
+    compute kernels without taking SMs from them (an NCCL gather runs kernels
+    that occupy whole SMs while it moves data).
+
+    Collective: every rank of ``group`` constructs it with the same ``shape``
+    and ``dtype``; the root allocates the buffer (``buffer`` on the root,
+    None elsewhere) and exports it, the other ranks map it.  ``ok`` is False on
+    every rank when any rank could not map it (no peer access between the
+    GPUs, or an allocation that cannot be exported); callers then keep their
+    NCCL path.  ``put(src, offset)`` queues one ``cudaMemcpyAsync`` of a
+    contiguous tensor to byte ``offset`` of the buffer on ``stream``; the
+    root's buffer holds the data once the writer's stream passed the copy,
+    which a later collective on that stream (``done``) makes known to the
+    root.  ``close()`` unmaps it (collective).
+    """
+
+    def __init__(self, shape, dtype, device, group=None, root: int = 0):
+        self.group, self.root = group, root
+        self.rank = dist.get_rank(group)
+        self.nbytes = int(torch.Size(shape).numel()) * torch.empty((), dtype=dtype).element_size()
+        self.buffer = None
+        self._peer_base = None
+        self._dst = 0
+        payload = [None]
+        if self.rank == root:
+            self.buffer = torch.empty(shape, dtype=dtype, device=device)
+            payload[0] = _export(self.buffer)
+            if payload[0] is not None:
+                self._dst = self.buffer.data_ptr()
+        src = dist.get_global_rank(group, root) if group is not None else root
+        dist.broadcast_object_list(payload, src=src, group=group)
+        mine = payload[0] is not None
+        if mine and self.rank != root:
+            handle, offset = payload[0]
+            self._peer_base = _open(handle)
+            mine = self._peer_base is not None
+            if mine:
+                self._dst = self._peer_base + offset
+        flags = [None] * dist.get_world_size(group)
+        dist.all_gather_object(flags, mine, group=group)
+        self.ok = all(flags)
+
+    def put(self, src: torch.Tensor, offset: int, stream: torch.cuda.Stream) -> None:
+        if not self.ok:
+            raise RuntimeError("RootWindow is not mapped on every rank")
+        if not src.is_contiguous():
+            raise ValueError("put needs a contiguous source")
+        nbytes = src.numel() * src.element_size()
+        if offset < 0 or offset + nbytes > self.nbytes:
+            raise ValueError("put outside the window")
+        from cuda.bindings import runtime as rt
+
+        (err,) = rt.cudaMemcpyAsync(self._dst + offset, src.data_ptr(), nbytes,
+                                    rt.cudaMemcpyKind.cudaMemcpyDeviceToDevice, stream.cuda_stream)
+        if err != rt.cudaError_t.cudaSuccess:
+            raise RuntimeError(f"cudaMemcpyAsync into the root window failed: {err}")
+
+    def done(self, device) -> None:
+        """On the current stream of every rank: after it, the root's stream sees
+        every copy that the ranks' current streams ordered before this call."""
+        flag = torch.zeros(1, device=device)
+        dist.all_reduce(flag, group=self.group)
+
+    def close(self) -> None:
+        if self._peer_base is not None:
+            from cuda.bindings import runtime as rt
+
+            torch.cuda.synchronize()
+            rt.cudaIpcCloseMemHandle(self._peer_base)
+            self._peer_base = None
+        dist.barrier(group=self.group)
+        self.buffer = None
+
+
+def _export(t: torch.Tensor):
+    """(IPC handle bytes, offset of ``t`` in its allocation), or None."""
+    try:
+        from cuda.bindings import driver as drv
+        from cuda.bindings import runtime as rt
+    except ImportError:
+        return None
+    err, base, _ = drv.cuMemGetAddressRange(drv.CUdeviceptr(t.data_ptr()))
+    if err != drv.CUresult.CUDA_SUCCESS:
+        return None
+    err, handle = rt.cudaIpcGetMemHandle(int(base))
+    if err != rt.cudaError_t.cudaSuccess:
+        return None
+    return bytes(handle.reserved), t.data_ptr() - int(base)
+
+
+def _open(handle_bytes: bytes):
+    try:
+        from cuda.bindings import runtime as rt
+    except ImportError:
+        return None
+    handle = rt.cudaIpcMemHandle_t()
+    handle.reserved = handle_bytes
+    err, ptr = rt.cudaIpcOpenMemHandle(handle, rt.cudaIpcMemLazyEnablePeerAccess)
+    if err != rt.cudaError_t.cudaSuccess:
+        return None
+    return int(ptr)
