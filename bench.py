@@ -575,10 +575,12 @@ def run_engine(args, rank: int, world: int, local_rank: int):
             "config": {
                 "workload": (f"{args.workload}: causal prefill bf16 B={B} H={H} D={D} T={T}, then {S} decode "
                              f"steps (KV append + split-K decode), (b,h) pairs sharded over {world} GPU(s), "
-                             "outputs gathered to rank 0 (with N > 1 the prefill runs in "
-                             f"{len(chunks)} query-row chunks, longest first, alternating over two streams, each chunk's output sent to rank 0 "
-                             f"while the next chunk computes, by {prefill_transport}; decode gathers over NCCL, "
-                             "queued and waited for at the end of the step)"),
+                             + ("one prefill launch, outputs stay on the GPU" if world == 1 else
+                                "outputs gathered to rank 0 (the prefill runs in "
+                                f"{len(chunks)} query-row chunks, longest first, alternating over two streams, "
+                                "each chunk's output sent to rank 0 while later chunks compute, by "
+                                f"{prefill_transport}; decode gathers over NCCL, queued and waited for at the end "
+                                "of the step)")),
                 "global_batch": B, "seq_len": T, "parallelism": f"bxh-shard{world}",
                 "l2": "inputs larger than L2 (Q/K/V/cache >= 8 GB per step)",
             },
@@ -635,29 +637,37 @@ def run_e2e(args, cfg, plan, rank, world, local_rank, q, kc, vc, qd, kd, vd, ws,
     dq = torch.empty_like(q)
     do = torch.empty_like(q)
     o_full = torch.empty(world, n, T, D, dtype=q.dtype, device=dev) if rank == 0 and world > 1 else None
-    dqd = torch.empty_like(qd)
+    # Decode inputs in two sets, by step parity, so a step's copy-in never
+    # overwrites what the previous step's last chunks still read.
+    dqd_sets = [torch.empty_like(qd) for _ in range(2)]
+    dkd_sets = [torch.empty_like(kd) for _ in range(2)]
+    dvd_sets = [torch.empty_like(vd) for _ in range(2)]
     dod = torch.empty_like(qd)
     od_full = torch.empty(S, world, n, 1, D, dtype=q.dtype, device=dev) if rank == 0 and world > 1 else None
 
     # (b,h) pairs are independent through prefill and decode, so the step runs chunk by chunk of
-    # pairs: chunk c's inputs land on a copy stream while chunk c-1 computes, then chunk c's
+    # pairs: chunk c's inputs land on a copy stream while earlier chunks compute, then chunk c's
     # prefill and its S decode steps run, and its prefill output goes back to the host on a
-    # second copy stream while chunk c+1 computes.  The decode inputs of every step (small) land
-    # first, the decode outputs go back at the end.  With N > 1 every rank's outputs are gathered
-    # to rank 0 after the last chunk and copied back from there.  The step ends when every copy
-    # has landed.
+    # second copy stream while later chunks compute.  Consecutive steps overlap the same way: a
+    # step's chunk c is copied in as soon as the previous step finished with chunk c (its prefill
+    # output copied out, its decode steps done), so the copy-in of one step runs under the compute
+    # of the previous one and the PCIe transfers, not the pipeline fill, bound the step.  The
+    # decode inputs (small) land first, in the set of the step's parity; the decode outputs go
+    # back at the end.  With N > 1 every rank's outputs are gathered to rank 0 after the last
+    # chunk and copied back from there.  Every step's copies are inside the timed region.
     n_chunks = max(1, min(8, n))
     bounds = [round(i * n / n_chunks) for i in range(n_chunks + 1)]
     compute = torch.cuda.current_stream(dev)
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    dkd, dvd = torch.empty_like(kd), torch.empty_like(vd)
     od_all = torch.empty((world * S,) + tuple(qd.shape[1:]), dtype=q.dtype, device=dev) if rank == 0 and world > 1 else None
     ho_v = ho.view(1, n, T, D) if world == 1 else None
+    chunk_free = [None] * n_chunks  # event: the previous step is done with chunk c
+    parity = [0]
 
     def step():
-        start = compute.record_event()
-        s_in.wait_event(start)
-        s_out.wait_event(start)
+        par = parity[0]
+        parity[0] ^= 1
+        dqd, dkd, dvd = dqd_sets[par], dkd_sets[par], dvd_sets[par]
         landed = []
         with torch.cuda.stream(s_in):
             dqd.copy_(hqd, non_blocking=True)
@@ -665,12 +675,16 @@ def run_e2e(args, cfg, plan, rank, world, local_rank, q, kc, vc, qd, kd, vd, ws,
             dvd.copy_(hvd, non_blocking=True)
             for c in range(n_chunks):
                 c0, c1 = bounds[c], bounds[c + 1]
+                if chunk_free[c] is not None:
+                    s_in.wait_event(chunk_free[c])
                 dq[:, c0:c1].copy_(hq[:, c0:c1], non_blocking=True)
                 kc[:, c0:c1, :T].copy_(hk[:, c0:c1], non_blocking=True)
                 vc[:, c0:c1, :T].copy_(hv[:, c0:c1], non_blocking=True)
                 landed.append(s_in.record_event())
         for c in range(n_chunks):
             c0, c1 = bounds[c], bounds[c + 1]
+            # landed[c] follows chunk_free[c] on the copy-in stream, so the previous
+            # step's copy-out of do[chunk c] has completed too.
             compute.wait_event(landed[c])
             engine.forward(dq[:, c0:c1], kc[:, c0:c1, :T], vc[:, c0:c1, :T], is_causal=True, need_lse=False,
                            out=do[:, c0:c1])
@@ -682,6 +696,10 @@ def run_e2e(args, cfg, plan, rank, world, local_rank, q, kc, vc, qd, kd, vd, ws,
                 engine.kv_append(dkd[s][:, c0:c1], dvd[s][:, c0:c1], kc[:, c0:c1], vc[:, c0:c1], position=T + s)
                 engine.decode(dqd[s][:, c0:c1], kc[:, c0:c1, : T + s + 1], vc[:, c0:c1, : T + s + 1], is_causal=True,
                               causal_offset=T + s, out=dod[s][:, c0:c1], workspace=ws)
+            # Chunk c is free for the next step once its decode steps ran and its
+            # prefill output left (the copy-out stream is in order).
+            s_out.wait_event(compute.record_event())
+            chunk_free[c] = s_out.record_event()
         if world > 1:
             gather(do, o_full)
             gather(dod, od_all)
@@ -720,8 +738,8 @@ def run_e2e(args, cfg, plan, rank, world, local_rank, q, kc, vc, qd, kd, vd, ws,
             "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h, "steps": steps,
             "path": "tensorsmith_b200.engine (C ABI) with pinned host inputs/outputs; the step runs in "
                     f"{n_chunks} chunks of (b,h) pairs: a chunk's inputs are copied in on a copy stream while "
-                    "the previous chunk's prefill and decode steps run, and its prefill output is copied back "
-                    "while the next chunk runs"}
+                    "earlier chunks (of this step or, for a step's first chunks, of the previous step) compute, "
+                    "and its prefill output is copied back while later chunks run"}
 
 
 def _timed(args, step, n_events):
