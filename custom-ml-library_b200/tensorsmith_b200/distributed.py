@@ -217,29 +217,35 @@ class RootWindow:
 
 
 def _export(t: torch.Tensor):
-    """(IPC handle bytes, offset of ``t`` in its allocation), or None."""
+    """(IPC handle bytes, offset of ``t`` in its allocation), or None when the
+    tensor cannot be exported (host memory, no CUDA driver, no cuda-python)."""
+    if not t.is_cuda:
+        return None
     try:
         from cuda.bindings import driver as drv
         from cuda.bindings import runtime as rt
-    except ImportError:
+
+        err, base, _ = drv.cuMemGetAddressRange(drv.CUdeviceptr(t.data_ptr()))
+        if err != drv.CUresult.CUDA_SUCCESS:
+            return None
+        err, handle = rt.cudaIpcGetMemHandle(int(base))
+        if err != rt.cudaError_t.cudaSuccess:
+            return None
+        return bytes(handle.reserved), t.data_ptr() - int(base)
+    except (ImportError, RuntimeError):
         return None
-    err, base, _ = drv.cuMemGetAddressRange(drv.CUdeviceptr(t.data_ptr()))
-    if err != drv.CUresult.CUDA_SUCCESS:
-        return None
-    err, handle = rt.cudaIpcGetMemHandle(int(base))
-    if err != rt.cudaError_t.cudaSuccess:
-        return None
-    return bytes(handle.reserved), t.data_ptr() - int(base)
 
 
 def _open(handle_bytes: bytes):
+    """Device address of the root's mapped allocation, or None."""
     try:
         from cuda.bindings import runtime as rt
-    except ImportError:
+
+        handle = rt.cudaIpcMemHandle_t()
+        handle.reserved = handle_bytes
+        err, ptr = rt.cudaIpcOpenMemHandle(handle, rt.cudaIpcMemLazyEnablePeerAccess)
+        if err != rt.cudaError_t.cudaSuccess:
+            return None
+        return int(ptr)
+    except (ImportError, RuntimeError):
         return None
-    handle = rt.cudaIpcMemHandle_t()
-    handle.reserved = handle_bytes
-    err, ptr = rt.cudaIpcOpenMemHandle(handle, rt.cudaIpcMemLazyEnablePeerAccess)
-    if err != rt.cudaError_t.cudaSuccess:
-        return None
-    return int(ptr)

@@ -114,3 +114,42 @@ def test_gather_to_root_single_rank():
     assert gather_to_root(local, plan, out=out2, async_op=True) is None and torch.equal(out2, local)
     with pytest.raises(ValueError):
         gather_to_root(local, plan, async_op=True)
+
+
+def _window_worker(rank, world, port, queue):
+    import torch.distributed as dist
+
+    from tensorsmith_b200.distributed import RootWindow
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=__import__("datetime").timedelta(seconds=20))
+    try:
+        # Host memory cannot be exported over CUDA IPC: every rank must learn
+        # that the window is unusable (and keep its NCCL path), none may hang.
+        window = RootWindow((64,), torch.float32, torch.device("cpu"))
+        mapped = window.ok
+        has_buffer = window.buffer is not None
+        refused = False
+        try:
+            window.put(torch.zeros(4), 0, None)
+        except RuntimeError:
+            refused = True
+        window.close()
+        queue.put(("ok", (not mapped) and has_buffer == (rank == 0) and refused))
+    except Exception as error:  # pragma: no cover - reported to the parent
+        queue.put(("error", repr(error)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_root_window_falls_back_together_world2():
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_window_worker, args=(r, 2, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [queue.get(timeout=60) for _ in procs]
+    for p in procs:
+        p.join(timeout=30)
+    assert all(kind == "ok" and flag for kind, flag in results), results
