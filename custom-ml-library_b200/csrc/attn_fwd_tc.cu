@@ -1075,13 +1075,18 @@ cudaError_t tc_forward(const ts_attn_params& p, uint32_t* fault, cudaStream_t st
   a.n_units = p.batch * p.q_heads * a.half_x;
   a.fault = fault;
   a.drop = drop ? *drop : DropoutArgs{};
-  // Two or more query tiles run on the two-tile kernel, which measured faster
-  // than both kernels of this file: C5 shape (T=32768) 1189 against 1066
-  // TFLOP/s, C3 (T=4096) 886 against 843 (persistent) and 790 (one tile).
+  // Without dropout, two or more query tiles run on the two-tile kernel, which
+  // measured faster than both kernels of this file: C5 shape (T=32768) 1189
+  // against 1066 TFLOP/s, C3 (T=4096) 886 against 843 (persistent) and 790
+  // (one tile).
   // A single query tile (short prefill chunks, the grouped-query decode view)
   // keeps the one-tile kernel.
+  // With dropout the one-tile kernels stay the default: the counter-based
+  // generator lengthens each warpgroup's softmax, which the two-tile kernel
+  // pays in full on its softmax -> P.V -> S chain (C3, p = 0.1: 362 against
+  // 422 TFLOP/s for the persistent one-tile kernel).
   const FwdKernel env = fwd_kernel_env();
-  if (a.n_q_tiles >= 2 && (env == FwdKernel::kDefault || env == FwdKernel::kPair))
+  if (a.n_q_tiles >= 2 && (env == FwdKernel::kPair || (env == FwdKernel::kDefault && a.drop.p == 0.f)))
     return tc_forward_pair(p, mq, mk, mv, fault, st, drop);
   const bool persistent = env == FwdKernel::kPersistent || (env == FwdKernel::kDefault && use_persistent(a, sm_count()));
   const bool bf = p.dtype == TS_BF16;

@@ -128,7 +128,7 @@ TC_CASES = [
     ("bfloat16", 1, 4, 2, 200, 331, 64, True, 131, 0.2),
     ("bfloat16", 2, 2, 2, 130, 130, 128, False, 0, 0.5),
     ("float16", 1, 2, 1, 257, 257, 128, True, 0, 0.1),
-    # 148 pairs x 2 units: with TS_FWD_KERNEL=persistent, the persistent forward's kDrop instantiation
+    # 148 pairs x 2 units: by default the persistent one-tile forward's kDrop instantiation
     ("bfloat16", 1, 148, 74, 300, 300, 64, True, 0, 0.2),
 ]
 
@@ -138,11 +138,11 @@ TC_CASES = [
 def test_tcgen05_dropout_matches_oracle(case, kernel, monkeypatch):
     """The tensor-core forward and backward (kDrop instantiations) draw the same
     mask as the materialised one and match the oracle's dense dropout VJP.
-    "default" runs the two-tile forward on these multi-tile shapes; "other"
-    selects the one-tile kernel (or the persistent one for the 148-pair case)."""
+    "default" runs the one-tile forward (persistent for the 148-pair case), the
+    default with dropout; "other" selects the two-tile kernel's kDrop variant."""
     name, b, hq, hkv, tq, tk, d, causal, offset, p = case
     if kernel == "other":
-        monkeypatch.setenv("TS_FWD_KERNEL", "persistent" if hq == 148 else "tile")
+        monkeypatch.setenv("TS_FWD_KERNEL", "pair")
     rng = np.random.default_rng(tq + tk + d)
     q, k, v = (rng.normal(size=s) for s in ((b, hq, tq, d), (b, hkv, tk, d), (b, hkv, tk, d)))
     g = rng.normal(size=(b, hq, tq, d))
