@@ -46,6 +46,8 @@ WORKLOADS = {
     "small": dict(batch=4, heads=32, head_dim=128, prefill=4096, decode_steps=4),
     # the C5 prefill shape on 8 (b,h) pairs (forward + backward, 268 MB of inputs): profiler captures
     "c5slice": dict(batch=1, heads=8, head_dim=128, prefill=32768, scale_inputs=False),
+    # causal attention forward + backward, fp32 (the exact CUDA-core kernels)
+    "c1": dict(batch=2, heads=4, head_dim=64, prefill=256),
     # causal prefill bf16 forward + backward
     "c3": dict(batch=8, heads=16, head_dim=128, prefill=4096, scale_inputs=True),
     # 4-layer decoder LM training step (fp16 autocast, fp32 params), B=16, T=256
@@ -959,6 +961,125 @@ def cpu_c2_attention_baseline(B, H, T, D, L, budget_s):
             "sample": f"oracle fwd+bwd of one (b,h) slice T={T} D={D}, median of {len(times)} reps, scaled x{B * H * L}"}
 
 
+def run_c1(args):
+    """Causal attention forward + backward in fp32, B=2 H=4 T=256 D=64, Q/K/V/dO ~ N(0,1) from seed 0
+    (the case tensorsmith runs on its NumPy CPU backend today): the exact fp32
+    CUDA-core kernels, checked in full against fp64."""
+    import torch
+
+    from tensorsmith_b200 import engine
+
+    cfg = WORKLOADS[args.workload]
+    B, H, T, D = cfg["batch"], cfg["heads"], cfg["prefill"], cfg["head_dim"]
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    q, k, v, do = (torch.randn(B, H, T, D, generator=gen, device=dev) for _ in range(4))
+    out = torch.empty_like(q)
+    lse = torch.empty(B, H, T, dtype=torch.float32, device=dev)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    path = engine.fwd_path(q, k, v, is_causal=True)
+
+    def step(ev):
+        ev[0].record()
+        engine.forward(q, k, v, is_causal=True, out=out, lse=lse)
+        ev[1].record()
+        engine.backward(q, k, v, out, lse, do, is_causal=True, dq=dq, dk=dk, dv=dv)
+        ev[2].record()
+
+    evs, eager_ms, clocks = _timed(args, step, 3)
+    fwd = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    bwd = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    pairs_flops = causal_flops(B * H, T, T, 0, D) / 4.0  # D * P
+    # At this size the step is bound by the host (the engine's Python/ctypes calls
+    # and launches), so the step is also captured once in a CUDA graph and replayed:
+    # the same kernels and buffers, launched without the host in the loop.
+    graph_note = "the forward and backward calls captured once in a CUDA graph, replayed per step"
+    try:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                step([torch.cuda.Event(enable_timing=True) for _ in range(3)])
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            engine.forward(q, k, v, is_causal=True, out=out, lse=lse)
+            engine.backward(q, k, v, out, lse, do, is_causal=True, dq=dq, dk=dk, dv=dv)
+        for _ in range(max(3, args.warmup)):
+            graph.replay()
+        torch.cuda.synchronize()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        g1.record()
+        torch.cuda.synchronize()
+        engine.check_device_status()
+        step_ms = g0.elapsed_time(g1) / args.steps
+    except Exception as error:  # capture refused: keep the eager timing
+        step_ms = eager_ms
+        graph_note = f"CUDA graph unavailable ({error!r}); eager calls timed"
+    value = 14.0 * pairs_flops / (step_ms / 1e3) / 1e12
+    # parity of the last timed step: every (b,h) slice in full against fp64 on the host
+    errs = {"out": 0.0, "lse": 0.0, "dq": 0.0, "dk": 0.0, "dv": 0.0}
+    peaks_ref = {"out": 0.0, "lse": 0.0, "dq": 0.0, "dk": 0.0, "dv": 0.0}
+    for bb in range(B):
+        for hh in range(H):
+            ref = ref_slice_backward(q[bb, hh].cpu(), k[bb, hh].cpu(), v[bb, hh].cpu(), do[bb, hh].cpu(), D ** -0.5)
+            for name, got, r in zip(("out", "lse", "dq", "dk", "dv"),
+                                    (out[bb, hh], lse[bb, hh], dq[bb, hh], dk[bb, hh], dv[bb, hh]), ref):
+                errs[name] = max(errs[name], max_abs(got, r))
+                peaks_ref[name] = max(peaks_ref[name], float(r.abs().max()))
+    rel = {name: errs[name] / max(1.0, peaks_ref[name]) for name in errs}
+    # nominal fp32 FMA rate of the CUDA cores: 148 SMs x 128 lanes x 2 FLOP x the maximum SM clock
+    fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+    return {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"c1: causal attention fp32 B={B} H={H} T={T} D={D}, forward + backward, "
+                               "Q/K/V/dO ~ N(0,1) from seed 0 (BASELINE config 0); " + graph_note,
+                   "l2": "inputs fit in L2 (1 MB); the step is launch-bound at this size"},
+        "eager": {"ms_per_step": eager_ms, "tflops": 14.0 * pairs_flops / (eager_ms / 1e3) / 1e12,
+                  "note": "the same calls from Python every step (host-bound)"},
+        "parity": {"max_abs": errs, "max_rel": rel, "tolerance_rel": 1e-4, "pass": max(rel.values()) <= 1e-4,
+                   "rows": "every (b,h) slice in full; fp64 reference on the host; errors relative to "
+                           "max(1, max|ref|)"},
+        "forward": {"tflops": 4.0 * pairs_flops / (fwd / 1e3) / 1e12, "ms": fwd, "path": path},
+        "backward": {"tflops": 10.0 * pairs_flops / (bwd / 1e3) / 1e12, "ms": bwd},
+        "roofline": {"bound": "fma", "kernel": "simt_fwd_kernel + simt_bwd_{delta,dq,dkdv} (exact fp32)",
+                     "achieved": value, "peak": fp32_peak, "unit": "TFLOP/s", "frac": value / fp32_peak,
+                     "peak_source": "nominal fp32 CUDA-core FMA rate at the maximum SM clock (no measured figure)",
+                     "traffic": None,
+                     "algorithmic": f"14*D*causal_pairs = {14 * pairs_flops:.4g} FLOP per step"},
+        "gpu_launches": 4 * args.steps,  # simt_fwd_kernel, simt_bwd_delta, simt_bwd_dq, simt_bwd_dkdv
+        "clocks": clocks,
+        **({} if args.no_cpu_baseline else {"cpu_baseline": cpu_c1_baseline(cfg, args.cpu_seconds)}),
+    }
+
+
+def cpu_c1_baseline(cfg, budget_s):
+    """The oracle (tensorsmith's NumPy algorithm) on the whole C1 problem: dense forward and VJP in fp32."""
+    import numpy as np
+
+    import oracle
+
+    B, H, T, D = cfg["batch"], cfg["heads"], cfg["prefill"], cfg["head_dim"]
+    rng = np.random.default_rng(0)
+    q, k, v, g = (rng.standard_normal((B, H, T, D)).astype(np.float32) for _ in range(4))
+    flops = 14.0 * causal_flops(B * H, T, T, 0, D) / 4.0
+    times, start = [], time.perf_counter()
+    while not times or (time.perf_counter() - start < budget_s and len(times) < 50):
+        t0 = time.perf_counter()
+        o, l = oracle.attention_forward(q, k, v, is_causal=True, algorithm="dense")
+        oracle.attention_backward(q, k, v, o, l, g, is_causal=True)
+        times.append(time.perf_counter() - t0)
+    return {"value": flops / statistics.median(times) / 1e12, "unit": "TFLOP/s", "cores": cpu_cores(),
+            "kind": "port", "sample": f"the whole C1 problem (B={B} H={H} T={T} D={D}), oracle dense forward + "
+                                      f"VJP in NumPy fp32, median of {len(times)} reps"}
+
+
 def cpu_c3_baseline(cfg, budget_s):
     """Oracle streaming forward + blockwise backward on one (b,h) slice, rows sub-sampled."""
     import numpy as np
@@ -1120,10 +1241,11 @@ def main():
         from tensorsmith_b200 import _lib
 
         build = {"lib": str(_lib.LIB_PATH.relative_to(ROOT)), "source_digest": _lib.library_digest()}
-        if args.workload in ("c2", "c3", "c5slice", "c4", "c4q", "c4q_small", "c4gqa"):
+        if args.workload in ("c1", "c2", "c3", "c5slice", "c4", "c4q", "c4q_small", "c4gqa"):
             if world > 1:
-                raise SystemExit("the c2 / c3 / c4 parity configs run on one GPU; c5 is the multi-GPU workload")
-            result = (run_c2(args) if args.workload == "c2" else run_c3(args) if args.workload in ("c3", "c5slice")
+                raise SystemExit("the c1 / c2 / c3 / c4 parity configs run on one GPU; c5 is the multi-GPU workload")
+            result = (run_c1(args) if args.workload == "c1" else run_c2(args) if args.workload == "c2"
+                      else run_c3(args) if args.workload in ("c3", "c5slice")
                       else run_c4(args, quantized=args.workload.startswith("c4q")))
         else:
             result = run_engine(args, rank, world, local_rank)

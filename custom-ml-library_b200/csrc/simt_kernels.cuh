@@ -34,6 +34,7 @@ template <typename A> struct SimtCfg {
 constexpr int kSimtThreads = 128;
 constexpr int kSimtKeys = 32;     // keys staged per shared-memory tile
 constexpr int kSimtQRows = 32;    // query rows staged per tile (dK/dV kernel)
+constexpr int kStageBatch = 8;    // global loads in flight per thread while staging a tile
 
 struct RowCtx {
   int b, h, hk, kv_end, offset;
@@ -84,9 +85,22 @@ __device__ __forceinline__ A group_sum(A x) {
 template <typename T, typename A>
 __device__ __forceinline__ void stage_rows(A* dst, const ts_view4& src, int b, int hk, int k0,
                                            int rows, int end, int C) {
-  for (int idx = threadIdx.x; idx < rows * C; idx += blockDim.x) {
-    const int r = idx / C, c = idx - r * C, t = k0 + r;
-    dst[idx] = t < end ? Elem<T>::to_acc(*at4<T>(src, b, hk, t, c)) : A(0);
+  // kStageBatch loads per thread are issued before any of them is stored, so
+  // their latencies overlap instead of adding up one element at a time.
+  const int n = rows * C;
+  for (int base = threadIdx.x; base < n; base += blockDim.x * kStageBatch) {
+    A tmp[kStageBatch];
+#pragma unroll
+    for (int u = 0; u < kStageBatch; ++u) {
+      const int idx = base + u * blockDim.x;
+      const int r = idx / C, c = idx - r * C, t = k0 + r;
+      tmp[u] = (idx < n && t < end) ? Elem<T>::to_acc(*at4<T>(src, b, hk, t, c)) : A(0);
+    }
+#pragma unroll
+    for (int u = 0; u < kStageBatch; ++u) {
+      const int idx = base + u * blockDim.x;
+      if (idx < n) dst[idx] = tmp[u];
+    }
   }
 }
 
@@ -344,14 +358,8 @@ __global__ void __launch_bounds__(kSimtThreads)
     const int h = hk * rep + r;
     for (int i0 = i_begin; i0 < p.q_len; i0 += kSimtQRows) {
       __syncthreads();
-      for (int idx = threadIdx.x; idx < kSimtQRows * D; idx += blockDim.x) {
-        const int rr = idx / D, c = idx - rr * D, i = i0 + rr;
-        qs[idx] = i < p.q_len ? Elem<T>::to_acc(*at4<T>(p.q, b, h, i, c)) : A(0);
-      }
-      for (int idx = threadIdx.x; idx < kSimtQRows * Dv; idx += blockDim.x) {
-        const int rr = idx / Dv, c = idx - rr * Dv, i = i0 + rr;
-        gs[idx] = i < p.q_len ? Elem<T>::to_acc(*at4<T>(bp.dout, b, h, i, c)) : A(0);
-      }
+      stage_rows<T, A>(qs, p.q, b, h, i0, kSimtQRows, p.q_len, D);
+      stage_rows<T, A>(gs, bp.dout, b, h, i0, kSimtQRows, p.q_len, Dv);
       if (threadIdx.x < kSimtQRows) {
         const int i = i0 + threadIdx.x;
         A lval = neg_inf<A>();
@@ -459,10 +467,33 @@ inline cudaError_t launch_bwd_g(const ts_attn_bwd_params& bp, typename Elem<T>::
   return cudaGetLastError();
 }
 
+// SMs of the current device (cached per device).
+inline int simt_sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    cached[dev] = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+// Threads per row: the fewest that cover the channels (more channels per
+// thread, fewer shuffles), widened while the grid of `rows` rows in `slices`
+// (batch x head) grids would leave SMs idle (small problems: the BASELINE C1
+// shape has 8 (b,h) slices of 256 rows).
+template <typename A> inline int simt_group_for(int dmax, int rows, int slices) {
+  int g = simt_group<A>(dmax);
+  const int64_t want = 2 * (int64_t)simt_sm_count();
+  while (g < 16 && (int64_t)ceil_div(rows, kSimtThreads / g) * slices < want) g <<= 1;
+  return g;
+}
+
 template <typename T>
 inline cudaError_t simt_fwd_t(const ts_attn_params& p, const DropoutArgs* drop, cudaStream_t st) {
   using A = typename Elem<T>::acc;
-  switch (simt_group<A>(max(p.head_dim, p.value_dim))) {
+  switch (simt_group_for<A>(max(p.head_dim, p.value_dim), p.q_len, p.batch * p.q_heads)) {
     case 1: return launch_fwd_g<T, 1>(p, drop, st);
     case 2: return launch_fwd_g<T, 2>(p, drop, st);
     case 4: return launch_fwd_g<T, 4>(p, drop, st);
@@ -476,7 +507,9 @@ template <typename T>
 inline cudaError_t simt_bwd_t(const ts_attn_bwd_params& bp, void* ws, const DropoutArgs* drop, cudaStream_t st) {
   using A = typename Elem<T>::acc;
   A* delta = reinterpret_cast<A*>(ws);
-  switch (simt_group<A>(max(bp.fwd.head_dim, bp.fwd.value_dim))) {
+  const ts_attn_params& p = bp.fwd;
+  switch (simt_group_for<A>(max(p.head_dim, p.value_dim), min(p.q_len, p.kv_len),
+                            p.batch * min(p.q_heads, p.kv_heads))) {
     case 1: return launch_bwd_g<T, 1>(bp, delta, drop, st);
     case 2: return launch_bwd_g<T, 2>(bp, delta, drop, st);
     case 4: return launch_bwd_g<T, 4>(bp, delta, drop, st);
