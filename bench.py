@@ -991,9 +991,9 @@ def run_c1(args):
     fwd = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
     bwd = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
     pairs_flops = causal_flops(B * H, T, T, 0, D) / 4.0  # D * P
-    # At this size the step is bound by the host (the engine's Python/ctypes calls
-    # and launches), so the step is also captured once in a CUDA graph and replayed:
-    # the same kernels and buffers, launched without the host in the loop.
+    # The step is also captured once in a CUDA graph and replayed (the same kernels
+    # and buffers without the host in the loop); `value` is the replayed step.  At
+    # this size the replay takes as long as the eager calls: the kernels bound it.
     graph_note = "the forward and backward calls captured once in a CUDA graph, replayed per step"
     try:
         side = torch.cuda.Stream(dev)
@@ -1040,9 +1040,9 @@ def run_c1(args):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"c1: causal attention fp32 B={B} H={H} T={T} D={D}, forward + backward, "
                                "Q/K/V/dO ~ N(0,1) from seed 0 (BASELINE config 0); " + graph_note,
-                   "l2": "inputs fit in L2 (1 MB); the step is launch-bound at this size"},
+                   "l2": "inputs fit in L2 (1 MB)"},
         "eager": {"ms_per_step": eager_ms, "tflops": 14.0 * pairs_flops / (eager_ms / 1e3) / 1e12,
-                  "note": "the same calls from Python every step (host-bound)"},
+                  "note": "the same calls from Python every step"},
         "parity": {"max_abs": errs, "max_rel": rel, "tolerance_rel": 1e-4, "pass": max(rel.values()) <= 1e-4,
                    "rows": "every (b,h) slice in full; fp64 reference on the host; errors relative to "
                            "max(1, max|ref|)"},
