@@ -135,7 +135,11 @@ TS_ATTN_API int ts_attn_fwd_path(const ts_attn_params* params, int decode);
 
 /* Prefill / training forward: O and (optionally) LSE.  Replaces the dense,
  * streaming and native forwards of nn/attention.py:132-198 (the native slot
- * :146-174 is where tensorsmith plugs a vendor kernel). */
+ * :146-174 is where tensorsmith plugs a vendor kernel).  On the tensor-core
+ * path the library picks the kernel by shape (two query tiles per CTA for two
+ * or more 128-row tiles); the environment variable TS_FWD_KERNEL = "pair",
+ * "tile" or "persistent", read at every call, forces one for tests and
+ * measurements.  Results are the same within the stated tolerances. */
 TS_ATTN_API int ts_attn_fwd(const ts_attn_params* params, void* stream);
 
 /* Workspace bytes ts_attn_bwd needs (fp32 row statistics, plus an fp32 dQ
